@@ -1,0 +1,141 @@
+/*
+ * ttt_attn.h - C ABI of libttt_attn.so, the sm_100a (B200) grad-grad-safe
+ * attention library.
+ *
+ * The library computes, per head, O = softmax(scale * Q K^T [causal mask]) V,
+ * the first-order gradients (dQ, dK, dV) for an upstream dO, and the complete
+ * second-order terms (the gradients of <dQ,u_q> + <dK,u_k> + <dV,u_v> with
+ * respect to Q, K, V and, optionally, dO).
+ *
+ * Conventions shared by every entry point:
+ *  - Tensors are [b, h, t, d] views in 16-bit floating point (fp16 or bf16),
+ *    given as a device pointer plus element strides of the b, h and t
+ *    dimensions; the d stride is 1. Strides must be positive multiples of 8
+ *    elements (16 bytes) and pointers 16-byte aligned.
+ *  - d must be 64 or 128.
+ *  - Row statistics (lse2, delta, gamma, rho) are fp32 arrays [b*h, t_pad]
+ *    with t_pad = ttt_attn_t_pad(t) = roundup(t, 128), owned by the caller.
+ *  - Nothing here allocates device memory; all buffers come from the caller.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream); no entry point synchronizes the host.
+ *  - Return value: TTT_OK or a ttt_status code. Argument errors are detected
+ *    on the host before anything is enqueued. `err` (optional, device int32)
+ *    receives a nonzero code if a kernel gave up on a bounded wait; the
+ *    caller reads it after synchronizing.
+ *
+ * Reference interface each entry point replaces (paths inside
+ * ry2009/TestTimeIdeas) is cited on the declaration.
+ */
+#ifndef TTT_ATTN_H_
+#define TTT_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTT_ATTN_ABI_VERSION 1
+
+enum ttt_status {
+  TTT_OK = 0,
+  TTT_ERR_NULL = 1,        /* a required pointer is NULL */
+  TTT_ERR_DTYPE = 2,       /* dtype is not TTT_F16 or TTT_BF16 */
+  TTT_ERR_HEAD_DIM = 3,    /* d is not 64 or 128 */
+  TTT_ERR_SHAPE = 4,       /* b, h or t out of range */
+  TTT_ERR_STRIDE = 5,      /* a stride is not a positive multiple of 8 elements */
+  TTT_ERR_ALIGN = 6,       /* a pointer is not 16-byte aligned */
+  TTT_ERR_TENSOR_MAP = 7,  /* the driver rejected a TMA tensor map */
+  TTT_ERR_LAUNCH = 8,      /* a kernel launch failed */
+  TTT_ERR_DRIVER = 9,      /* the driver entry point for tensor maps is unavailable */
+  TTT_ERR_UNSUPPORTED = 10 /* valid request this build does not implement */
+};
+
+enum ttt_dtype { TTT_F16 = 0, TTT_BF16 = 1 };
+
+typedef struct {
+  void* ptr;          /* device address of element [0, 0, 0, 0] */
+  int64_t sb, sh, st; /* element strides of the b, h and t dimensions */
+} ttt_view;
+
+typedef struct {
+  int32_t b, h, t, d;
+  int32_t dtype;  /* enum ttt_dtype */
+  int32_t causal; /* nonzero: key j is visible to query i only if j <= i */
+  float scale;    /* softmax scale; callers map scale=None to 1/sqrt(d) */
+} ttt_problem;
+
+/* Forward. Writes o and lse2 (base-2 log-sum-exp of scale*log2(e)*q k^T per
+ * row; rows t..t_pad-1 get +inf). If p != NULL also writes the normalized
+ * probabilities P as [b*h, t, t] 16-bit row-major (entries of causal key tiles
+ * past the diagonal tile are left unwritten).
+ * Replaces: ttt_kernels/triton_attention.py:278-337 (_attn_fwd_kernel,
+ * _attn_fwd_kernel_stats, _attn_probs_kernel launches) and the probability
+ * forward of the save_p modes, triton_attention.py:51-59 and 270-273. */
+typedef struct {
+  ttt_problem pb;
+  ttt_view q, k, v;
+  ttt_view o;
+  float* lse2;
+  void* p;
+  int32_t* err;
+} ttt_fwd_args;
+int ttt_attn_fwd(const ttt_fwd_args* a, void* stream);
+
+/* First-order backward for upstream gradient dout. Writes delta =
+ * rowsum(dout o o) (fp32 [b*h, t_pad], consumed by ttt_attn_bwd2) and dq, dk,
+ * dv. P is recomputed from lse2.
+ * Replaces: backward_stubs.py:154-181 (triton_attn_bwd_dv_from_p),
+ * :224-255 (triton_attn_rowsum_from_p), :362-425 (triton_attn_bwd_dqdk_from_p)
+ * and the recompute backward of triton_attention.py:416-420. */
+typedef struct {
+  ttt_problem pb;
+  ttt_view q, k, v, o, dout;
+  const float* lse2;
+  float* delta;
+  ttt_view dq, dk, dv;
+  int32_t* err;
+} ttt_bwd_args;
+int ttt_attn_bwd(const ttt_bwd_args* a, void* stream);
+
+/* Double backward. Given the probes uq, uk, uv (upstream gradients of dq, dk,
+ * dv), writes gq, gk, gv = d<dq,uq>+<dk,uk>+<dv,uv> / d(q, k, v) and, if
+ * gdout.ptr != NULL, the gradient with respect to dout. gamma and rho are
+ * caller-owned fp32 [b*h, t_pad] scratch rows.
+ * Replaces: backward_stubs.py:435-439 (TritonDvFn.backward), :450-459
+ * (TritonRowSumFn.backward), :471-514 (TritonDqDkFn.backward) and the stubs
+ * triton_attn_bwd2_dq / _dk / _dv, backward_stubs.py:539-548. Unlike those,
+ * the terms through P's dependence on q and k are included. */
+typedef struct {
+  ttt_problem pb;
+  ttt_view q, k, v, dout;
+  const float* lse2;
+  const float* delta;
+  ttt_view uq, uk, uv;
+  float* gamma;
+  float* rho;
+  ttt_view gq, gk, gv;
+  ttt_view gdout;
+  int32_t* err;
+} ttt_bwd2_args;
+int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream);
+
+/* roundup(t, 128): the row count of every statistics array. */
+int ttt_attn_t_pad(int t);
+/* Static description of a status code. */
+const char* ttt_attn_status_string(int status);
+/* TTT_ATTN_ABI_VERSION of the loaded library. */
+int ttt_attn_abi_version(void);
+
+/* Test hook (no reference counterpart): one 128 x n x k tcgen05 GEMM,
+ * c[128 x n] (fp32, row-major) = a[128 x k] * b, with b given as [n x k]
+ * (b_mn_major = 0) or [k x n] (b_mn_major = 1), all row-major and contiguous.
+ * n in {64, 128, 256}, k in {64, 128}. */
+int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn_major,
+                           int32_t* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTT_ATTN_H_ */

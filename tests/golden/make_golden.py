@@ -1,0 +1,94 @@
+"""Generate the golden vectors in tests/golden/ from the reference itself.
+
+Runs only where the reference checkout exists (default /root/reference, or
+$TTT_REFERENCE_DIR). It imports the reference's ``ttt_kernels`` package under
+the alias ``ref_ttt_kernels`` (its own name is taken by the drop-in package of
+this repository) and calls its public entry point
+``triton_attention(q, k, v, causal=..., bwd_mode=...)`` on CPU tensors, where
+the reference runs its math path (triton_attention.py:275-280 forward,
+416-420 recompute backward). Outputs: forward O, first-order grads of
+<O, dO> (create_graph=True) and second-order grads of <dq,uq>+<dk,uk>+<dv,uv>.
+
+Also records the reference's ``save_p`` mode on the same inputs; its
+grad-grad for q and k differs from the math path because P is saved as a
+constant (backward_stubs.py:428-514); the tests pin that difference too.
+
+    python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import math
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("TTT_REFERENCE_DIR", "/root/reference"))
+
+# (name, b, h, t, d, causal, dtype, seed, input scale)
+CASES = [
+    ("config1_noncausal_t64_d64_fp32", 1, 1, 64, 64, False, torch.float32, 0, 1.0),
+    ("config1_causal_t64_d64_fp32", 1, 1, 64, 64, True, torch.float32, 1, 1.0),
+    ("ragged_causal_b2h2_t37_d16_fp64", 2, 2, 37, 16, True, torch.float64, 2, 1.0),
+    ("noncausal_b1h2_t48_d16_fp64", 1, 2, 48, 16, False, torch.float64, 3, 1.0),
+    ("causal_b1h1_t130_d16_fp64", 1, 1, 130, 16, True, torch.float64, 4, 0.5),
+    ("noncausal_b1h1_t64_d128_fp32", 1, 1, 64, 128, False, torch.float32, 5, 0.5),
+]
+
+
+def load_reference():
+    pkg_dir = REF / "ttt_kernels"
+    spec = importlib.util.spec_from_file_location("ref_ttt_kernels", pkg_dir / "__init__.py",
+                                                  submodule_search_locations=[str(pkg_dir)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["ref_ttt_kernels"] = mod
+    spec.loader.exec_module(mod)
+    # the package re-exports the function under the submodule's name
+    return sys.modules["ref_ttt_kernels.triton_attention"]
+
+
+def run_reference(ta, inputs, causal, mode):
+    q, k, v = (inputs[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    out = ta.triton_attention(q, k, v, causal=causal, bwd_mode=mode)
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), inputs["do"], create_graph=True)
+    l2 = (dq * inputs["uq"]).sum() + (dk * inputs["uk"]).sum() + (dv * inputs["uv"]).sum()
+    gq, gk, gv = torch.autograd.grad(l2, (q, k, v))
+    return {"o": out, "dq": dq, "dk": dk, "dv": dv, "gq": gq, "gk": gk, "gv": gv}
+
+
+def run_reference_mean_loss(ta, inputs, causal):
+    """The reference benchmark objective (tests/bench_gradgrad_sweep.py:56-61)."""
+    q, k, v = (inputs[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    out = ta.triton_attention(q, k, v, causal=causal, bwd_mode="recompute")
+    grads = torch.autograd.grad(out.float().mean(), (q, k, v), create_graph=True)
+    s = sum(g.pow(2).mean() for g in grads)
+    gg = torch.autograd.grad(s, (q, k, v))
+    return {"gq": gg[0], "gk": gg[1], "gv": gg[2]}
+
+
+def main() -> None:
+    ta = load_reference()
+    for name, b, h, t, d, causal, dtype, seed, sc in CASES:
+        g = torch.Generator().manual_seed(seed)
+        inputs = {n: (torch.randn(b, h, t, d, generator=g, dtype=torch.float64) * sc).to(dtype)
+                  for n in ("q", "k", "v", "do", "uq", "uk", "uv")}
+        ref = run_reference(ta, inputs, causal, "recompute")
+        rec = {f"in_{n}": x.numpy() for n, x in inputs.items()}
+        rec.update({f"ref_{n}": x.detach().numpy() for n, x in ref.items()})
+        savep = run_reference(ta, inputs, causal, "save_p")
+        rec.update({f"savep_{n}": x.detach().numpy() for n, x in savep.items() if n.startswith("g")})
+        ml = run_reference_mean_loss(ta, inputs, causal)
+        rec.update({f"meanloss_{n}": x.detach().numpy() for n, x in ml.items()})
+        rec["meta"] = np.array([b, h, t, d, int(causal), seed], dtype=np.int64)
+        rec["scale"] = np.array(1.0 / math.sqrt(d))
+        np.savez_compressed(HERE / f"{name}.npz", **rec)
+        print(f"wrote {name}.npz")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,233 @@
+"""GPU parity tests: the sm_100a kernels (called through the C ABI of
+libttt_attn.so) against the CPU oracle on identical seeded inputs.
+
+Tolerance (from the path's specification): max-abs error <= 2e-3 for fp16 and
+<= 1e-2 for bf16 against a float reference, measured here as
+max|x - ref| / max(1, max|ref|) so that outputs with magnitude above 1 are
+held to the same relative accuracy. The reference is the oracle evaluated in
+float64 on the same 16-bit-rounded inputs. Causal-mask structure is checked
+exactly (zero tolerance).
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import attention_oracle as orc
+from testtimeideas_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+NAMES = ("q", "k", "v", "do", "uq", "uk", "uv")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _library():
+    lib = _lib.load_library()  # raises if the extension was not built: no fallback
+    yield lib
+    _lib.check_device_errors()
+
+
+def _cuda_inputs(b, h, t, d, dtype, seed, scale_in=0.5):
+    inp = orc.seeded_inputs(b, h, t, d, seed=seed, scale_in=scale_in)
+    return {n: x.to(dtype).cuda() for n, x in inp.items()}
+
+
+def _oracle(inp, causal, need_gdo=False):
+    cpu = {n: x.detach().cpu().double() for n, x in inp.items()}
+    return orc.math_gradgrad(*(cpu[n] for n in NAMES), causal=causal, need_gdo=need_gdo)
+
+
+def _assert_close(x, ref, dtype, name):
+    err = orc.normalized_err(x.detach().float().cpu(), ref)
+    assert err <= TOL[dtype], f"{name}: normalized max-abs error {err:.3e} > {TOL[dtype]:.0e}"
+
+
+# ---------------------------------------------------------------- descriptor self-test
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("n", [64, 128, 256])
+@pytest.mark.parametrize("k", [64, 128])
+def test_selftest_umma(dtype, b_mn, n, k):
+    g = torch.Generator().manual_seed(n * 7 + k)
+    a = torch.randn(128, k, generator=g).to(dtype).cuda()
+    b = torch.randn(k, n, generator=g).to(dtype).cuda() if b_mn else torch.randn(n, k, generator=g).to(dtype).cuda()
+    c = _lib.selftest_umma(a, b, b_mn)
+    ref = a.float() @ (b.float() if b_mn else b.float().t())
+    torch.cuda.synchronize()
+    assert (c - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
+# ---------------------------------------------------------------- op-level parity
+SHAPES = [(1, 1, 64), (1, 2, 128), (2, 1, 200), (1, 1, 257), (1, 2, 512)]
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"b{b}h{h}t{t}" for b, h, t in SHAPES])
+def test_forward_parity(d, dtype, causal, shape):
+    b, h, t = shape
+    inp = _cuda_inputs(b, h, t, d, dtype, seed=t + d)
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], causal, scale)
+    ref = orc.closed_form_gradgrad(*(inp[n].cpu().double().numpy() for n in NAMES), causal=causal, scale=scale)
+    _assert_close(o, ref["o"], dtype, "o")
+    lse = (lse2[:, :t].cpu().double() * math.log(2.0)).reshape(b, h, t)
+    assert orc.max_abs_err(lse, ref["lse"]) <= 1e-3
+    assert torch.isinf(lse2[:, t:]).all()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"b{b}h{h}t{t}" for b, h, t in SHAPES])
+def test_backward_parity(d, dtype, causal, shape):
+    b, h, t = shape
+    inp = _cuda_inputs(b, h, t, d, dtype, seed=2 * t + d)
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], causal, scale)
+    dq, dk, dv, delta = _lib.attn_bwd(inp["q"], inp["k"], inp["v"], o, inp["do"], lse2, causal, scale)
+    ref = _oracle(inp, causal)
+    for name, x in (("dq", dq), ("dk", dk), ("dv", dv)):
+        _assert_close(x, ref[name], dtype, name)
+    assert (delta[:, t:] == 0).all()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"b{b}h{h}t{t}" for b, h, t in SHAPES])
+def test_double_backward_parity(d, dtype, causal, shape):
+    b, h, t = shape
+    inp = _cuda_inputs(b, h, t, d, dtype, seed=3 * t + d)
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], causal, scale)
+    _, _, _, delta = _lib.attn_bwd(inp["q"], inp["k"], inp["v"], o, inp["do"], lse2, causal, scale)
+    gq, gk, gv, gdo = _lib.attn_bwd2(inp["q"], inp["k"], inp["v"], inp["do"], lse2, delta, inp["uq"], inp["uk"],
+                                     inp["uv"], causal, scale, need_gdout=True)
+    ref = _oracle(inp, causal, need_gdo=True)
+    for name, x in (("gq", gq), ("gk", gk), ("gv", gv), ("gdo", gdo)):
+        _assert_close(x, ref[name], dtype, name)
+
+
+# ---------------------------------------------------------------- public API
+@pytest.mark.parametrize("mode", ["recompute", "recompute_manual", "save_p", "save_p_triton_full", "dv_only",
+                                  "custom"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_public_api_gradgrad(mode, causal):
+    import ttt_kernels
+    dtype = torch.float16
+    inp = _cuda_inputs(1, 2, 192, 64, dtype, seed=17)
+    q, k, v = (inp[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    o = ttt_kernels.triton_attention(q, k, v, causal=causal, bwd_mode=mode)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), inp["do"], create_graph=True)
+    gq, gk, gv = torch.autograd.grad((dq, dk, dv), (q, k, v), (inp["uq"], inp["uk"], inp["uv"]))
+    ref = _oracle(inp, causal)
+    for name, x in zip(("o", "dq", "dk", "dv", "gq", "gk", "gv"), (o, dq, dk, dv, gq, gk, gv)):
+        _assert_close(x, ref[name], dtype, name)
+
+
+def test_public_api_reference_objective():
+    """The reference benchmark's objective: loss = mean(O), s = sum mean(g^2)."""
+    import ttt_kernels
+    dtype = torch.float16
+    inp = _cuda_inputs(1, 1, 256, 64, dtype, seed=19, scale_in=1.0)
+    q, k, v = (inp[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    out = ttt_kernels.triton_attention(q, k, v, causal=True, bwd_mode="save_p_triton_full")
+    grads = torch.autograd.grad(out.float().mean(), (q, k, v), create_graph=True)
+    s = sum(g.float().pow(2).mean() for g in grads)
+    gg = torch.autograd.grad(s, (q, k, v))
+    ref = orc.mean_loss_gradgrad(*(inp[n].cpu() for n in ("q", "k", "v")), causal=True)
+    for name, x in zip(("gq", "gk", "gv"), gg):
+        r = ref[name]
+        err = orc.max_abs_err(x.float().cpu(), r) / float(r.abs().max())
+        assert err <= 2e-2, (name, err)  # grads of 1/numel-scaled losses sit near fp16's subnormal range
+
+
+def test_dout_requires_grad_path():
+    import ttt_kernels
+    dtype = torch.bfloat16
+    inp = _cuda_inputs(2, 2, 160, 128, dtype, seed=23)
+    q, k, v = (inp[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    w = inp["do"].clone().requires_grad_(True)
+    o = ttt_kernels.triton_attention(q, k, v, causal=True)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), w, create_graph=True)
+    gq, gk, gv, gw = torch.autograd.grad((dq, dk, dv), (q, k, v, w), (inp["uq"], inp["uk"], inp["uv"]))
+    ref = _oracle(inp, True, need_gdo=True)
+    for name, x in zip(("gq", "gk", "gv", "gdo"), (gq, gk, gv, gw)):
+        _assert_close(x, ref[name], dtype, name)
+
+
+def test_strided_bthd_layout():
+    """[b, t, h, d] memory viewed as [b, h, t, d] feeds TMA without a copy."""
+    dtype = torch.float16
+    b, h, t, d = 2, 3, 150, 64
+    base = {n: x.to(dtype).cuda() for n, x in orc.seeded_inputs(b, t, h, d, seed=29, scale_in=0.5).items()}
+    inp = {n: x.transpose(1, 2) for n, x in base.items()}
+    assert _lib.prep(inp["q"]) is inp["q"]
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], True, scale)
+    dq, dk, dv, delta = _lib.attn_bwd(inp["q"], inp["k"], inp["v"], o, inp["do"], lse2, True, scale)
+    gq, gk, gv, _ = _lib.attn_bwd2(inp["q"], inp["k"], inp["v"], inp["do"], lse2, delta, inp["uq"], inp["uk"],
+                                   inp["uv"], True, scale, need_gdout=False)
+    ref = _oracle(inp, True)
+    for name, x in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv), ("gq", gq), ("gk", gk), ("gv", gv)):
+        _assert_close(x, ref[name], dtype, name)
+
+
+def test_causal_mask_structure_exact():
+    """Rows i < m never see keys j >= m: with dO zero on rows >= m, every
+    gradient on keys/values >= m is exactly zero, first and second order."""
+    dtype = torch.float16
+    b, h, t, d, m = 1, 2, 300, 64, 137
+    inp = _cuda_inputs(b, h, t, d, dtype, seed=31)
+    inp["do"][:, :, m:] = 0
+    inp["uq"][:, :, m:] = 0
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], True, scale)
+    dq, dk, dv, delta = _lib.attn_bwd(inp["q"], inp["k"], inp["v"], o, inp["do"], lse2, True, scale)
+    assert int((dk[:, :, m:] != 0).sum()) == 0
+    assert int((dv[:, :, m:] != 0).sum()) == 0
+    # perturbing future keys leaves earlier outputs bit-identical
+    k2 = inp["k"].clone()
+    k2[:, :, m:] += 1.0
+    o2, _, _ = _lib.attn_fwd(inp["q"], k2, inp["v"], True, scale)
+    assert torch.equal(o[:, :, :m], o2[:, :, :m])
+
+
+def test_save_p_probabilities():
+    dtype = torch.float16
+    b, h, t, d = 1, 2, 256, 64
+    inp = _cuda_inputs(b, h, t, d, dtype, seed=37)
+    scale = 1.0 / math.sqrt(d)
+    o, lse2, p = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], True, scale, save_p=True)
+    ref = orc.closed_form_gradgrad(*(inp[n].cpu().double().numpy() for n in NAMES), causal=True, scale=scale)
+    s = (inp["q"].double() @ inp["k"].double().transpose(-1, -2)) * scale
+    pr = torch.softmax(s.masked_fill(torch.triu(torch.ones(t, t, dtype=torch.bool, device=s.device), 1),
+                                     float("-inf")), -1)
+    tri = torch.tril(torch.ones(t, t, dtype=torch.bool, device=p.device))
+    assert (p.double() - pr)[..., tri].abs().max().item() <= 2e-3
+    # inside the visible tile band every entry above the diagonal is exactly zero
+    band = torch.triu(torch.ones(t, t, dtype=torch.bool, device=p.device), 1) & \
+        (torch.arange(t, device=p.device)[None, :] // 128 <= torch.arange(t, device=p.device)[:, None] // 128)
+    assert int((p[..., band] != 0).sum()) == 0
+    _assert_close(o, ref["o"], dtype, "o")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_config2_shape_fwd_bwd(causal):
+    """b=2 h=4 T=2048 d=128 fp16 (the reference's forward/backward benchmark shape);
+    reference: the oracle's math path evaluated in float32 on the device."""
+    dtype = torch.float16
+    inp = _cuda_inputs(2, 4, 2048, 128, dtype, seed=41)
+    scale = 1.0 / math.sqrt(128)
+    o, lse2, _ = _lib.attn_fwd(inp["q"], inp["k"], inp["v"], causal, scale)
+    dq, dk, dv, _ = _lib.attn_bwd(inp["q"], inp["k"], inp["v"], o, inp["do"], lse2, causal, scale)
+    q, k, v = (inp[n].float().requires_grad_(True) for n in ("q", "k", "v"))
+    ref_o = orc.attention_math(q, k, v, causal, scale)
+    rdq, rdk, rdv = torch.autograd.grad(ref_o, (q, k, v), inp["do"].float())
+    for name, x, r in (("o", o, ref_o), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        _assert_close(x, r.detach().cpu(), dtype, name)

@@ -1,0 +1,267 @@
+"""ctypes binding of libttt_attn.so (include/ttt_attn.h) and the tensor-level ops.
+
+Every op here runs the sm_100a kernels; there is no CPU or PyTorch fallback:
+if the library is missing or the tensors are not CUDA fp16/bf16 with
+d in {64, 128}, the op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "_lib" / "libttt_attn.so"
+
+TTT_F16, TTT_BF16 = 0, 1
+_STATUS = {
+    0: "ok", 1: "null pointer", 2: "dtype", 3: "head dim", 4: "shape", 5: "stride", 6: "alignment",
+    7: "tensor map", 8: "launch", 9: "driver entry point", 10: "unsupported",
+}
+
+
+class View(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("sb", ctypes.c_int64), ("sh", ctypes.c_int64), ("st", ctypes.c_int64)]
+
+
+class Problem(ctypes.Structure):
+    _fields_ = [("b", ctypes.c_int32), ("h", ctypes.c_int32), ("t", ctypes.c_int32), ("d", ctypes.c_int32),
+                ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_float)]
+
+
+class FwdArgs(ctypes.Structure):
+    _fields_ = [("pb", Problem), ("q", View), ("k", View), ("v", View), ("o", View),
+                ("lse2", ctypes.c_void_p), ("p", ctypes.c_void_p), ("err", ctypes.c_void_p)]
+
+
+class BwdArgs(ctypes.Structure):
+    _fields_ = [("pb", Problem), ("q", View), ("k", View), ("v", View), ("o", View), ("dout", View),
+                ("lse2", ctypes.c_void_p), ("delta", ctypes.c_void_p),
+                ("dq", View), ("dk", View), ("dv", View), ("err", ctypes.c_void_p)]
+
+
+class Bwd2Args(ctypes.Structure):
+    _fields_ = [("pb", Problem), ("q", View), ("k", View), ("v", View), ("dout", View),
+                ("lse2", ctypes.c_void_p), ("delta", ctypes.c_void_p),
+                ("uq", View), ("uk", View), ("uv", View),
+                ("gamma", ctypes.c_void_p), ("rho", ctypes.c_void_p),
+                ("gq", View), ("gk", View), ("gv", View), ("gdout", View), ("err", ctypes.c_void_p)]
+
+
+# Every symbol include/ttt_attn.h declares.
+EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
+            "ttt_attn_abi_version", "ttt_attn_selftest_umma")
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load libttt_attn.so (once). Raises if it has not been built."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p} not found: build the CUDA library first (python -m testtimeideas_b200.build)")
+        lib = ctypes.CDLL(str(p))
+        for name in ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2"):
+            getattr(lib, name).restype = ctypes.c_int
+            getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.ttt_attn_t_pad.restype = ctypes.c_int
+        lib.ttt_attn_t_pad.argtypes = [ctypes.c_int]
+        lib.ttt_attn_status_string.restype = ctypes.c_char_p
+        lib.ttt_attn_status_string.argtypes = [ctypes.c_int]
+        lib.ttt_attn_abi_version.restype = ctypes.c_int
+        lib.ttt_attn_selftest_umma.restype = ctypes.c_int
+        lib.ttt_attn_selftest_umma.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                               ctypes.c_void_p]
+        if path is None:
+            _lib = lib
+        return lib
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = load_library().ttt_attn_status_string(status).decode()
+        raise KernelError(f"libttt_attn: {msg} (status {status})")
+
+
+def t_pad(t: int) -> int:
+    return (t + 127) // 128 * 128
+
+
+# ---------------------------------------------------------------- device error word
+_err_words: dict[int, torch.Tensor] = {}
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _err_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _err_words[idx] = w
+    return w
+
+
+def check_device_errors(device: torch.device | None = None) -> None:
+    """Synchronize and raise if any kernel on `device` gave up on a bounded wait."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    w = error_word(dev)
+    torch.cuda.synchronize(dev)
+    code = int(w.item())
+    if code != 0:
+        w.zero_()
+        raise KernelError(f"libttt_attn kernel timeout on {dev} (error word 0x{code:08x})")
+
+
+_SYNC_CHECK = os.environ.get("TTT_ATTN_SYNC_CHECK", "0") == "1"
+
+
+# ---------------------------------------------------------------- argument plumbing
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return TTT_F16
+    if t.dtype == torch.bfloat16:
+        return TTT_BF16
+    raise TypeError(f"ttt attention kernels take fp16 or bf16 tensors, got {t.dtype}")
+
+
+def prep(x: torch.Tensor) -> torch.Tensor:
+    """Return x, or a contiguous copy when its layout cannot feed a TMA tensor map
+    (d stride != 1, a stride not a multiple of 8 elements, or a misaligned base)."""
+    if x.dim() != 4:
+        raise ValueError(f"expected a [b, h, t, d] tensor, got shape {tuple(x.shape)}")
+    b, h, t, d = x.shape
+    ok = x.stride(3) == 1 and x.data_ptr() % 16 == 0
+    if ok:
+        for size, stride in ((b, x.stride(0)), (h, x.stride(1)), (t, x.stride(2))):
+            if size > 1 and (stride <= 0 or stride % 8 != 0):
+                ok = False
+    return x if ok else x.contiguous()
+
+
+def view(x: torch.Tensor | None) -> View:
+    if x is None:
+        return View(None, 0, 0, 0)
+    return View(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2))
+
+
+def problem(q: torch.Tensor, causal: bool, scale: float) -> Problem:
+    b, h, t, d = q.shape
+    return Problem(b, h, t, d, _dtype_code(q), 1 if causal else 0, float(scale))
+
+
+def validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("ttt attention kernels need CUDA tensors")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError(f"q, k, v must share one [b, h, t, d] shape, got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("q, k, v must share one dtype")
+    _dtype_code(q)
+    if q.shape[-1] not in (64, 128):
+        raise ValueError(f"head dim must be 64 or 128, got {q.shape[-1]}")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, v must be on one device")
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def default_scale(d: int) -> float:
+    return 1.0 / math.sqrt(d)
+
+
+# ---------------------------------------------------------------- ops
+def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False):
+    """O, lse2 (fp32 [b*h, t_pad]) and, with save_p, P ([b, h, t, t])."""
+    validate(q, k, v)
+    lib = load_library()
+    q, k, v = prep(q), prep(k), prep(v)
+    b, h, t, d = q.shape
+    with torch.cuda.device(q.device):
+        o = torch.empty((b, h, t, d), dtype=q.dtype, device=q.device)
+        lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
+        p = torch.empty((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
+        args = FwdArgs(problem(q, causal, scale), view(q), view(k), view(v), view(o), lse2.data_ptr(),
+                       p.data_ptr() if p is not None else None, error_word(q.device).data_ptr())
+        _check(lib.ttt_attn_fwd(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(q.device)
+    return o, lse2, p
+
+
+def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float):
+    """dq, dk, dv and delta = rowsum(dout o o) (fp32 [b*h, t_pad])."""
+    validate(q, k, v)
+    lib = load_library()
+    q, k, v, o, dout = prep(q), prep(k), prep(v), prep(o), prep(dout.to(q.dtype))
+    b, h, t, d = q.shape
+    with torch.cuda.device(q.device):
+        dq, dk, dv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
+        delta = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
+        args = BwdArgs(problem(q, causal, scale), view(q), view(k), view(v), view(o), view(dout),
+                       lse2.data_ptr(), delta.data_ptr(), view(dq), view(dk), view(dv),
+                       error_word(q.device).data_ptr())
+        _check(lib.ttt_attn_bwd(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(q.device)
+    return dq, dk, dv, delta
+
+
+def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float, need_gdout: bool):
+    """Second-order gradients gq, gk, gv (and gdout when requested, else None)."""
+    validate(q, k, v)
+    lib = load_library()
+    q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
+    zeros = None
+
+    def probe(u):
+        nonlocal zeros
+        if u is None:
+            if zeros is None:
+                zeros = torch.zeros_like(q, memory_format=torch.contiguous_format)
+            return zeros
+        return prep(u.to(q.dtype))
+
+    uq, uk, uv = probe(uq), probe(uk), probe(uv)
+    b, h, t, d = q.shape
+    with torch.cuda.device(q.device):
+        gq, gk, gv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
+        gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
+        gamma = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
+        rho = torch.empty_like(gamma)
+        args = Bwd2Args(problem(q, causal, scale), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
+                        delta.data_ptr(), view(uq), view(uk), view(uv), gamma.data_ptr(), rho.data_ptr(),
+                        view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr())
+        _check(lib.ttt_attn_bwd2(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(q.device)
+    return gq, gk, gv, gdout
+
+
+def selftest_umma(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool) -> torch.Tensor:
+    """c = a @ (b if b_mn_major else b.T) on one tcgen05 tile (test hook)."""
+    lib = load_library()
+    a, b = a.contiguous(), b.contiguous()
+    k = a.shape[1]
+    n = b.shape[1] if b_mn_major else b.shape[0]
+    c = torch.empty((128, n), dtype=torch.float32, device=a.device)
+    _check(lib.ttt_attn_selftest_umma(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, k, _dtype_code(a),
+                                      1 if b_mn_major else 0, error_word(a.device).data_ptr(), _stream()))
+    return c

@@ -1,0 +1,97 @@
+"""Build libttt_attn.so (the sm_100a kernels + C ABI) in-tree with nvcc.
+
+The library is written to ``testtimeideas_b200/_lib/libttt_attn.so`` and
+object files to ``testtimeideas_b200/_build/``; both are git-ignored build
+products. Usage::
+
+    python -m testtimeideas_b200.build            # incremental
+    python -m testtimeideas_b200.build --force    # rebuild everything
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+INCLUDE = PKG.parent / "include"
+BUILD = PKG / "_build"
+LIBDIR = PKG / "_lib"
+LIB = LIBDIR / "libttt_attn.so"
+
+SOURCES = ["capi.cu", "attn_fwd.cu", "attn_bwd_qm.cu", "attn_bwd_km.cu", "misc.cu"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+         "-Xptxas", "-warn-spills"]
+
+
+def nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found; the CUDA toolkit is required to build libttt_attn.so")
+    return cand
+
+
+def _headers() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+
+
+def _stale(obj: Path, src: Path) -> bool:
+    if not obj.exists():
+        return True
+    t = obj.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in [src, *_headers()])
+
+
+def _compile(src: Path, obj: Path, extra: list[str]) -> tuple[Path, str]:
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", str(CSRC), "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return obj, r.stderr
+
+
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
+    """Compile every CUDA source for sm_100a and link the shared library."""
+    extra = list(extra or [])
+    BUILD.mkdir(parents=True, exist_ok=True)
+    LIBDIR.mkdir(parents=True, exist_ok=True)
+    jobs = []
+    for name in SOURCES:
+        src = CSRC / name
+        obj = BUILD / (name + ".o")
+        if force or _stale(obj, src):
+            jobs.append((src, obj))
+    if jobs:
+        workers = min(len(jobs), max(1, os.cpu_count() or 1))
+        with cf.ThreadPoolExecutor(workers) as ex:
+            for obj, log in ex.map(lambda j: _compile(j[0], j[1], extra), jobs):
+                if verbose and log.strip():
+                    print(f"[{obj.name}]\n{log}", file=sys.stderr)
+    objs = [BUILD / (n + ".o") for n in SOURCES]
+    if force or jobs or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
+        tmp = LIB.with_suffix(".so.tmp")
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    args = ap.parse_args()
+    print(build(force=args.force, verbose=args.verbose))
+
+
+if __name__ == "__main__":
+    main()

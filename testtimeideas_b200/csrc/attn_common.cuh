@@ -1,0 +1,96 @@
+// Kernel-side parameter block and helpers shared by the forward, backward and
+// double-backward attention kernels.
+//
+// Data layout in HBM (per head bh = b*H + h):
+//   Q, K, V, dO, u_q, u_k, u_v : [b, h, T, d] 16-bit, arbitrary b/h/t strides
+//                                (multiples of 8 elements), unit d stride;
+//                                read only through TMA tensor maps.
+//   lse2, delta, gamma, rho    : fp32 [b*h, t_pad], t_pad = roundup(T, 128).
+//                                lse2 is the row log-sum-exp in base 2 of
+//                                scale*log2(e)*Q K^T; rows in [T, t_pad) hold
+//                                +inf (lse2) or 0 (the others).
+//   outputs (O, dq, dk, dv, ...): [b, h, T, d] 16-bit with given strides.
+#pragma once
+
+#include "tc100.cuh"
+
+namespace ttt {
+
+// Which pass a generic backward kernel instance runs.
+enum Kind : int {
+  kBwdQ = 0,     // dQ (query-major)
+  kStats = 1,    // gamma, rho row statistics of the double backward (query-major)
+  kBwd2Q = 2,    // dd_q (+ dd_dO) of the double backward (query-major)
+  kBwdKV = 3,    // dK, dV (key-major)
+  kBwd2KV = 4,   // dd_k, dd_v of the double backward (key-major)
+};
+
+struct KParams {
+  // Owner-side tiles (128 rows, resident for the whole CTA) and streamed tiles
+  // (BN rows per step). Which tensor sits in which slot depends on the pass.
+  CUtensorMap own[4];
+  CUtensorMap str[4];
+  // fp32 [b*h, t_pad] row statistics streamed per column tile (key-major).
+  CUtensorMap st[4];
+  // Raw row statistics (query-major kernels read their own rows directly).
+  const float* lse2;
+  const float* delta;
+  const float* gamma;
+  const float* rho;
+  // fp32 outputs (forward: lse2; stats pass: gamma, rho).
+  float* out_f0;
+  float* out_f1;
+  // 16-bit outputs.
+  uint16_t* out0;
+  int64_t o0_sb, o0_sh, o0_st;
+  uint16_t* out1;
+  int64_t o1_sb, o1_sh, o1_st;
+  int B, H, T, t_pad;
+  float scale;       // softmax scale applied to Q K^T
+  float scale_log2;  // scale * log2(e)
+  int* err;          // device error word (0 = ok), may be null
+};
+
+// Dynamic shared memory is only guaranteed 16-byte aligned; the 128-byte
+// swizzle atoms need 1024-byte alignment.
+TTT_DEV uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Time-bounded wait used only while draining after an abort: it ignores the
+// abort flag (the CTA is already aborting) but still gives up after the limit.
+TTT_DEV void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_test(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) return;
+  }
+}
+
+// Store 32 fp32 values (a row segment) as 16-bit to global memory, 16-byte stores.
+template <bool BF16>
+TTT_DEV void store_global32(uint16_t* dst, const float* v, float mul) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack2<BF16>(v[q * 8 + 0] * mul, v[q * 8 + 1] * mul);
+    w.y = pack2<BF16>(v[q * 8 + 2] * mul, v[q * 8 + 3] * mul);
+    w.z = pack2<BF16>(v[q * 8 + 4] * mul, v[q * 8 + 5] * mul);
+    w.w = pack2<BF16>(v[q * 8 + 6] * mul, v[q * 8 + 7] * mul);
+    reinterpret_cast<uint4*>(dst)[q] = w;
+  }
+}
+
+// Copy a [128 x D] fp32 accumulator from TMEM (columns col0..col0+D-1, lane =
+// row) to a 16-bit global row, scaled by `mul`. All 32 lanes of the warp must
+// call this (tcgen05.ld is warp-collective); only rows with `valid` store.
+template <int D, bool BF16>
+TTT_DEV void acc_to_global(uint32_t taddr_row, uint16_t* dst_row, bool valid, float mul) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    float v[32];
+    tmem_ld32(taddr_row + c * 32, v);
+    if (valid) store_global32<BF16>(dst_row + c * 32, v, mul);
+  }
+}
+
+}  // namespace ttt

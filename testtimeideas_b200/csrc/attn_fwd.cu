@@ -1,0 +1,319 @@
+// Forward attention kernel (sm_100a): O = softmax(scale * Q K^T) V, plus the
+// base-2 row log-sum-exp that the backward passes recompute P from.
+//
+// Replaces the Triton forward kernels of the reference
+// (ttt_kernels/triton_attention.py:86-256: _attn_fwd_kernel,
+// _attn_fwd_kernel_stats, _attn_probs_kernel) and the PyTorch math forward of
+// the save_p modes (triton_attention.py:51-59, 270-273).
+//
+// One CTA owns 128 query rows of one head and streams 128-key tiles:
+//   warp 5      TMA producer: Q once, then K/V tiles into a 2-stage ring.
+//   warp 4      MMA issuer:   S_n = Q K_n^T into TMEM (double buffered), then
+//                             O += P_n V_n into a TMEM accumulator.
+//   warps 0..3  softmax:      thread r owns query row r (TMEM lane r): reads
+//                             S_n, keeps the running max / sum, writes the
+//                             16-bit P_n tile into shared memory, and rescales
+//                             its O row in TMEM only when the running max grew
+//                             by more than 2^8 (so P stays <= 256).
+// Causal: key tiles past the diagonal are never loaded or multiplied; the
+// diagonal tile is masked elementwise.
+// save_p: after the main loop the CTA recomputes S for each visible tile and
+// writes the normalized P (16-bit, row-major [T, T] per head) to HBM.
+#include "attn_common.cuh"
+#include "kernels.h"
+
+namespace ttt {
+
+template <int D, bool SAVE_P>
+struct FwdCfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int TILE_Q = BM * D * 2;
+  static constexpr int TILE_KV = BN * D * 2;
+  static constexpr int TILE_P = BM * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + TILE_Q;
+  static constexpr int OFF_V = OFF_K + 2 * TILE_KV;
+  static constexpr int OFF_P = OFF_V + 2 * TILE_KV;
+  static constexpr int OFF_BAR = OFF_P + 2 * TILE_P;
+  static constexpr int NBAR = 16;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static_assert(SMEM <= 232448, "forward tile set exceeds shared memory");
+};
+
+template <int D, bool BF16, bool CAUSAL, bool SAVE_P>
+__global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
+  using C = FwdCfg<D, SAVE_P>;
+  constexpr int BM = C::BM, BN = C::BN, NP = D / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sK0 = smem + C::OFF_K;
+  uint8_t* sV0 = smem + C::OFF_V;
+  uint8_t* sP0 = smem + C::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // [2]
+  uint64_t* pv_done = bars + 9;   // [2]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int bidx = bh / p.H, hidx = bh % p.H;
+  const int qblk = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.y;  // longest rows first
+  const int q0 = qblk * BM;
+  const int T = p.T;
+  const int n_all = (T + BN - 1) / BN;
+  const int n_tiles = CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 12; ++i) mbar_init(bars + i, 1);
+    mbar_init(p_full + 0, 128);
+    mbar_init(p_full + 1, 128);
+    // A nonzero error word means an earlier CTA or launch gave up: exit at once.
+    *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (*abort_flag) return;
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;        // S buffers at columns 0 and 128
+  const uint32_t tO = tmem + 256;  // O accumulator, D columns
+  Guard g{abort_flag, p.err};
+
+  if (warp == 5) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch(&p.own[0]);
+      tma_prefetch(&p.str[0]);
+      tma_prefetch(&p.str[1]);
+      int issued[2] = {0, 0};
+      mbar_arrive_tx(q_full, C::TILE_Q);
+      for (int pp = 0; pp < NP; ++pp) tma_load_4d(sQ + pp * BM * 128, &p.own[0], q_full, pp * 64, q0, hidx, bidx);
+      const int passes = SAVE_P ? 2 : 1;
+      int n_glob = 0;
+      for (int pass = 0; pass < passes; ++pass) {
+        for (int n = 0; n < n_tiles; ++n, ++n_glob) {
+          const int s = n_glob & 1;
+          if (n_glob >= 2 && !mbar_wait(kv_empty + s, ((n_glob - 2) >> 1) & 1, g, 1)) goto prod_done;
+          const bool need_v = (pass == 0);
+          mbar_arrive_tx(kv_full + s, need_v ? 2 * C::TILE_KV : C::TILE_KV);
+          for (int pp = 0; pp < NP; ++pp)
+            tma_load_4d(sK0 + s * C::TILE_KV + pp * BN * 128, &p.str[0], kv_full + s, pp * 64, n * BN, hidx, bidx);
+          if (need_v)
+            for (int pp = 0; pp < NP; ++pp)
+              tma_load_4d(sV0 + s * C::TILE_KV + pp * BN * 128, &p.str[1], kv_full + s, pp * 64, n * BN, hidx,
+                          bidx);
+          issued[s] = n_glob + 1;
+        }
+      }
+    prod_done:
+      // Wait for every load this thread issued before the CTA may exit.
+      mbar_drain(q_full, 0);
+      for (int s = 0; s < 2; ++s)
+        if (issued[s] > 0) mbar_drain(kv_full + s, ((issued[s] - 1) >> 1) & 1);
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(128, BN, BF16, false, false);
+      constexpr uint32_t id_o = idesc_f16(128, D, BF16, false, true);
+      bool ok = mbar_wait(q_full, 0, g, 2);
+      auto issue_s = [&](int n_glob, int buf) -> bool {
+        const int s = n_glob & 1;
+        if (!mbar_wait(kv_full + s, (n_glob >> 1) & 1, g, 3)) return false;
+        tc_fence_after();
+        const uint32_t aq = smem_u32(sQ), bk = smem_u32(sK0 + s * C::TILE_KV);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tS + buf * 128, desc_kmajor(aq, BM, kk), desc_kmajor(bk, BN, kk), id_s, kk > 0);
+        umma_commit(s_full + buf);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      for (int n = 0; ok && n < n_tiles; ++n) {
+        if (n + 1 < n_tiles && !issue_s(n + 1, (n + 1) & 1)) { ok = false; break; }
+        const int b = n & 1;
+        if (!mbar_wait(p_full + b, (n >> 1) & 1, g, 4)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ap = smem_u32(sP0 + b * C::TILE_P), bv = smem_u32(sV0 + b * C::TILE_KV);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_ss(tO, desc_kmajor(ap, BM, kk), desc_mnmajor(bv, BN, kk), id_o, (n > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(pv_done + b);
+        umma_commit(kv_empty + b);
+      }
+      if (SAVE_P && ok) {
+        // Second pass: S tiles again (K only), buffers keep alternating.
+        for (int n = 0; ok && n < n_tiles; ++n) {
+          const int n_glob = n_tiles + n;
+          const int buf = n_glob & 1;
+          // buffer `buf` was last read by the softmax warps for tile n_glob-2
+          if (n_glob >= 2 && !mbar_wait(p_full + buf, ((n_glob - 2) >> 1) & 1, g, 5)) { ok = false; break; }
+          if (!issue_s(n_glob, buf)) { ok = false; break; }
+          umma_commit(kv_empty + (n_glob & 1));
+        }
+      }
+      // Drain: every tcgen05 op issued above must finish before TMEM is freed.
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps 0..3
+    const int r = threadIdx.x;  // query row within the block == TMEM lane
+    const int row = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const float c = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int n = 0; n < n_tiles; ++n) {
+      const int b = n & 1;
+      if (!mbar_wait(s_full + b, (n >> 1) & 1, g, 6)) { ok = false; break; }
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int q = 0; q < BN / 32; ++q)
+        tmem_ld32(tS + lane_off + b * 128 + q * 32, *reinterpret_cast<float(*)[32]>(sv + q * 32));
+      const int k0 = n * BN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < BN; ++j) {
+        const int col = k0 + j;
+        const bool keep = (col < T) && (!CAUSAL || col <= row);
+        const float x = keep ? sv[j] * c : -INFINITY;
+        sv[j] = x;
+        mx = fmaxf(mx, x);
+      }
+      if (n == 0) {
+        m_used = mx;
+      } else {
+        const float m_new = fmaxf(m_used, mx);
+        const bool need = m_new > m_used + 8.f;
+        if (__any_sync(0xffffffffu, need)) {
+          // O may only be touched once the previous P V product has landed.
+          if (!mbar_wait(pv_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 7)) { ok = false; break; }
+          tc_fence_after();
+          const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
+          if (need) {
+            l *= alpha;
+            m_used = m_new;
+          }
+#pragma unroll
+          for (int q = 0; q < D / 16; ++q) {
+            float o[16];
+            tmem_ld16(tO + lane_off + q * 16, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tmem_st16(tO + lane_off + q * 16, o);
+          }
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < BN; ++j) {
+        sv[j] = fast_exp2(sv[j] - m_used);
+        rs += sv[j];
+      }
+      l += rs;
+      // P buffer b was read by the P V product of tile n-2.
+      if (n >= 2 && !mbar_wait(pv_done + b, ((n - 2) >> 1) & 1, g, 8)) { ok = false; break; }
+      uint8_t* tileP = sP0 + b * C::TILE_P;
+      store_row64<BF16>(tileP, BM, r, 0, sv);
+      store_row64<BF16>(tileP, BM, r, 64, sv + 64);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full + b);
+    }
+    if (ok && mbar_wait(pv_done + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, g, 9)) {
+      tc_fence_after();
+      const bool valid = row < T;
+      const float inv_l = 1.f / l;
+      uint16_t* orow = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
+                       static_cast<int64_t>(row) * p.o0_st;
+      acc_to_global<D, BF16>(tO + lane_off, orow, valid, inv_l);
+      const float lse2 = m_used + __log2f(l);
+      p.out_f0[static_cast<int64_t>(bh) * p.t_pad + row] = valid ? lse2 : INFINITY;
+      if (SAVE_P) {
+        // Normalized P for every visible tile: P = 2^(S*c - lse2).
+        uint16_t* prow = reinterpret_cast<uint16_t*>(p.out1) + static_cast<int64_t>(bh) * T * T +
+                         static_cast<int64_t>(row) * T;
+        for (int n = 0; n < n_tiles; ++n) {
+          const int n_glob = n_tiles + n;
+          const int b = n_glob & 1;
+          if (!mbar_wait(s_full + b, (n_glob >> 1) & 1, g, 10)) break;
+          tc_fence_after();
+          const int k0 = n * BN;
+#pragma unroll
+          for (int q = 0; q < BN / 32; ++q) {
+            float v[32];
+            tmem_ld32(tS + lane_off + b * 128 + q * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = k0 + q * 32 + j;
+              const bool keep = (col < T) && (!CAUSAL || col <= row);
+              v[j] = keep ? fast_exp2(v[j] * c - lse2) : 0.f;
+            }
+            if (valid) {
+              const int cbase = k0 + q * 32;
+              if (cbase + 32 <= T && (T & 7) == 0) {
+                store_global32<BF16>(prow + cbase, v, 1.f);
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (cbase + j < T) {
+                    const uint32_t w = pack2<BF16>(v[j], 0.f);
+                    prow[cbase + j] = static_cast<uint16_t>(w & 0xffffu);
+                  }
+              }
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(p_full + b);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+template <int D, bool BF16, bool CAUSAL, bool SAVE_P>
+static cudaError_t launch_fwd_t(const KParams& p, cudaStream_t stream) {
+  using C = FwdCfg<D, SAVE_P>;
+  auto kern = attn_fwd_kernel<D, BF16, CAUSAL, SAVE_P>;
+  static bool configured = false;  // per-instantiation; attribute is per-device but idempotent
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  configured = true;
+  (void)configured;
+  dim3 grid(p.B * p.H, (p.T + C::BM - 1) / C::BM);
+  kern<<<grid, 192, C::SMEM, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fwd(const KParams& p, int d, bool bf16, bool causal, bool save_p, cudaStream_t stream) {
+#define TTT_FWD_CASE(D_, BF_, CA_, SP_) \
+  if (d == D_ && bf16 == BF_ && causal == CA_ && save_p == SP_) return launch_fwd_t<D_, BF_, CA_, SP_>(p, stream);
+#define TTT_FWD_SP(D_, BF_, CA_) TTT_FWD_CASE(D_, BF_, CA_, false) TTT_FWD_CASE(D_, BF_, CA_, true)
+#define TTT_FWD_CA(D_, BF_) TTT_FWD_SP(D_, BF_, false) TTT_FWD_SP(D_, BF_, true)
+  TTT_FWD_CA(64, false) TTT_FWD_CA(64, true) TTT_FWD_CA(128, false) TTT_FWD_CA(128, true)
+#undef TTT_FWD_CA
+#undef TTT_FWD_SP
+#undef TTT_FWD_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ttt

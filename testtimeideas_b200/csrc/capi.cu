@@ -1,0 +1,338 @@
+// extern "C" entry points of libttt_attn.so: argument validation, TMA tensor
+// map encoding and the launch sequence of each pass. Declarations and the
+// contract live in include/ttt_attn.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "../../include/ttt_attn.h"
+#include "kernels.h"
+
+namespace {
+
+using ttt::KParams;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int check_problem(const ttt_problem& pb) {
+  if (pb.dtype != TTT_F16 && pb.dtype != TTT_BF16) return TTT_ERR_DTYPE;
+  if (pb.d != 64 && pb.d != 128) return TTT_ERR_HEAD_DIM;
+  if (pb.b < 1 || pb.h < 1 || pb.t < 1) return TTT_ERR_SHAPE;
+  if (pb.t > (1 << 22)) return TTT_ERR_SHAPE;
+  if (static_cast<int64_t>(pb.b) * pb.h > 0x7fffffff) return TTT_ERR_SHAPE;
+  return TTT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_view(const ttt_view& v, const ttt_problem& pb) {
+  if (v.ptr == nullptr) return TTT_ERR_NULL;
+  if (!aligned16(v.ptr)) return TTT_ERR_ALIGN;
+  const int64_t s[3] = {v.sb, v.sh, v.st};
+  const int64_t n[3] = {pb.b, pb.h, pb.t};
+  for (int i = 0; i < 3; ++i) {
+    if (n[i] == 1) continue;  // stride of a size-1 dimension is never used
+    if (s[i] <= 0 || (s[i] % 8) != 0) return TTT_ERR_STRIDE;
+  }
+  if (pb.t > 1 && v.st < pb.d) return TTT_ERR_STRIDE;
+  return TTT_OK;
+}
+
+int check_stats(const float* p) {
+  if (p == nullptr) return TTT_ERR_NULL;
+  if (!aligned16(p)) return TTT_ERR_ALIGN;
+  return TTT_OK;
+}
+
+// 4-D map over a [b, h, t, d] view: dims (d, t, h, b), box (64, rows, 1, 1),
+// 128-byte swizzle, out-of-bounds rows read as zero.
+int encode_view(CUtensorMap* m, const ttt_view& v, const ttt_problem& pb, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TTT_ERR_DRIVER;
+  // Size-1 dimensions get the contiguous stride so the driver sees a valid map.
+  int64_t st = pb.t > 1 ? v.st : pb.d;
+  int64_t sh = pb.h > 1 ? v.sh : st * pb.t;
+  int64_t sb = pb.b > 1 ? v.sb : sh * pb.h;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(pb.d), static_cast<cuuint64_t>(pb.t),
+                        static_cast<cuuint64_t>(pb.h), static_cast<cuuint64_t>(pb.b)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st * 2), static_cast<cuuint64_t>(sh * 2),
+                           static_cast<cuuint64_t>(sb * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      pb.dtype == TTT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, 4, v.ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
+}
+
+// 2-D map over fp32 statistics [bh, t_pad], box (64, 1).
+int encode_stats(CUtensorMap* m, const float* p, int bh, int t_pad) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TTT_ERR_DRIVER;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(t_pad), static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(t_pad) * 4};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
+}
+
+void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
+  k.B = pb.b;
+  k.H = pb.h;
+  k.T = pb.t;
+  k.t_pad = ttt_attn_t_pad(pb.t);
+  k.scale = pb.scale;
+  k.scale_log2 = pb.scale * 1.4426950408889634f;
+  k.err = err;
+}
+
+void set_out0(KParams& k, const ttt_view& v) {
+  k.out0 = static_cast<uint16_t*>(v.ptr);
+  k.o0_sb = v.sb;
+  k.o0_sh = v.sh;
+  k.o0_st = v.st;
+}
+void set_out1(KParams& k, const ttt_view& v) {
+  k.out1 = static_cast<uint16_t*>(v.ptr);
+  k.o1_sb = v.sb;
+  k.o1_sh = v.sh;
+  k.o1_st = v.st;
+}
+
+#define TTT_TRY(expr)          \
+  do {                         \
+    const int _s = (expr);     \
+    if (_s != TTT_OK) return _s; \
+  } while (0)
+
+int launched(cudaError_t e) { return e == cudaSuccess ? TTT_OK : TTT_ERR_LAUNCH; }
+
+}  // namespace
+
+extern "C" {
+
+int ttt_attn_t_pad(int t) { return (t + 127) / 128 * 128; }
+
+int ttt_attn_abi_version(void) { return TTT_ATTN_ABI_VERSION; }
+
+const char* ttt_attn_status_string(int s) {
+  switch (s) {
+    case TTT_OK: return "ok";
+    case TTT_ERR_NULL: return "a required pointer is NULL";
+    case TTT_ERR_DTYPE: return "dtype must be fp16 or bf16";
+    case TTT_ERR_HEAD_DIM: return "head dim d must be 64 or 128";
+    case TTT_ERR_SHAPE: return "b, h or t out of range";
+    case TTT_ERR_STRIDE: return "strides must be positive multiples of 8 elements with unit d stride";
+    case TTT_ERR_ALIGN: return "pointers must be 16-byte aligned";
+    case TTT_ERR_TENSOR_MAP: return "the driver rejected a TMA tensor map";
+    case TTT_ERR_LAUNCH: return "kernel launch failed";
+    case TTT_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable";
+    case TTT_ERR_UNSUPPORTED: return "unsupported request";
+    default: return "unknown status";
+  }
+}
+
+int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  TTT_TRY(check_view(a->q, pb));
+  TTT_TRY(check_view(a->k, pb));
+  TTT_TRY(check_view(a->v, pb));
+  TTT_TRY(check_view(a->o, pb));
+  TTT_TRY(check_stats(a->lse2));
+  if (a->p != nullptr && !aligned16(a->p)) return TTT_ERR_ALIGN;
+  KParams k;
+  std::memset(&k, 0, sizeof(k));
+  fill_common(k, pb, a->err);
+  TTT_TRY(encode_view(&k.own[0], a->q, pb, 128));
+  TTT_TRY(encode_view(&k.str[0], a->k, pb, 128));
+  TTT_TRY(encode_view(&k.str[1], a->v, pb, 128));
+  set_out0(k, a->o);
+  k.out_f0 = a->lse2;
+  k.out1 = static_cast<uint16_t*>(a->p);
+  return launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr,
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  const ttt_view* views[] = {&a->q, &a->k, &a->v, &a->o, &a->dout, &a->dq, &a->dk, &a->dv};
+  for (const ttt_view* v : views) TTT_TRY(check_view(*v, pb));
+  TTT_TRY(check_stats(a->lse2));
+  TTT_TRY(check_stats(a->delta));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = pb.dtype == TTT_BF16, causal = pb.causal != 0;
+  const int t_pad = ttt_attn_t_pad(pb.t), bh = pb.b * pb.h;
+
+  ttt::DeltaArgs da;
+  da.o = static_cast<const uint16_t*>(a->o.ptr);
+  da.o_sb = a->o.sb;
+  da.o_sh = a->o.sh;
+  da.o_st = a->o.st;
+  da.dout = static_cast<const uint16_t*>(a->dout.ptr);
+  da.d_sb = a->dout.sb;
+  da.d_sh = a->dout.sh;
+  da.d_st = a->dout.st;
+  da.delta = a->delta;
+  da.B = pb.b;
+  da.H = pb.h;
+  da.T = pb.t;
+  da.t_pad = t_pad;
+  da.D = pb.d;
+  da.bf16 = bf16;
+  TTT_TRY(launched(ttt::launch_delta(da, s)));
+
+  // dK, dV: key-major.
+  {
+    KParams k;
+    std::memset(&k, 0, sizeof(k));
+    fill_common(k, pb, a->err);
+    TTT_TRY(encode_view(&k.own[0], a->k, pb, 128));
+    TTT_TRY(encode_view(&k.own[1], a->v, pb, 128));
+    TTT_TRY(encode_view(&k.str[0], a->q, pb, 64));
+    TTT_TRY(encode_view(&k.str[1], a->dout, pb, 64));
+    TTT_TRY(encode_stats(&k.st[0], a->lse2, bh, t_pad));
+    TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad));
+    set_out0(k, a->dk);
+    set_out1(k, a->dv);
+    TTT_TRY(launched(ttt::launch_km(k, pb.d, bf16, causal, ttt::kBwdKV, s)));
+  }
+  // dQ: query-major.
+  {
+    KParams k;
+    std::memset(&k, 0, sizeof(k));
+    fill_common(k, pb, a->err);
+    TTT_TRY(encode_view(&k.own[0], a->q, pb, 128));
+    TTT_TRY(encode_view(&k.own[1], a->dout, pb, 128));
+    TTT_TRY(encode_view(&k.str[0], a->k, pb, 64));
+    TTT_TRY(encode_view(&k.str[1], a->v, pb, 64));
+    k.lse2 = a->lse2;
+    k.delta = a->delta;
+    set_out0(k, a->dq);
+    TTT_TRY(launched(ttt::launch_qm(k, pb.d, bf16, causal, ttt::kBwdQ, false, s)));
+  }
+  return TTT_OK;
+}
+
+int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  const ttt_view* views[] = {&a->q, &a->k, &a->v, &a->dout, &a->uq, &a->uk, &a->uv, &a->gq, &a->gk, &a->gv};
+  for (const ttt_view* v : views) TTT_TRY(check_view(*v, pb));
+  const bool gdo = a->gdout.ptr != nullptr;
+  if (gdo) TTT_TRY(check_view(a->gdout, pb));
+  TTT_TRY(check_stats(a->lse2));
+  TTT_TRY(check_stats(a->delta));
+  TTT_TRY(check_stats(a->gamma));
+  TTT_TRY(check_stats(a->rho));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = pb.dtype == TTT_BF16, causal = pb.causal != 0;
+  const int t_pad = ttt_attn_t_pad(pb.t), bh = pb.b * pb.h;
+
+  // Query-major: row statistics, then dd_q (+ dd_dout).
+  KParams kq;
+  std::memset(&kq, 0, sizeof(kq));
+  fill_common(kq, pb, a->err);
+  TTT_TRY(encode_view(&kq.own[0], a->q, pb, 128));
+  TTT_TRY(encode_view(&kq.own[1], a->dout, pb, 128));
+  TTT_TRY(encode_view(&kq.own[2], a->uq, pb, 128));
+  TTT_TRY(encode_view(&kq.str[0], a->k, pb, 64));
+  TTT_TRY(encode_view(&kq.str[1], a->v, pb, 64));
+  TTT_TRY(encode_view(&kq.str[2], a->uk, pb, 64));
+  TTT_TRY(encode_view(&kq.str[3], a->uv, pb, 64));
+  kq.lse2 = a->lse2;
+  kq.delta = a->delta;
+  kq.out_f0 = a->gamma;
+  kq.out_f1 = a->rho;
+  TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kStats, false, s)));
+  kq.gamma = a->gamma;
+  kq.rho = a->rho;
+  kq.out_f0 = nullptr;
+  kq.out_f1 = nullptr;
+  set_out0(kq, a->gq);
+  if (gdo) set_out1(kq, a->gdout);
+  TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s)));
+
+  // Key-major: dd_k, dd_v.
+  KParams kk;
+  std::memset(&kk, 0, sizeof(kk));
+  fill_common(kk, pb, a->err);
+  TTT_TRY(encode_view(&kk.own[0], a->k, pb, 128));
+  TTT_TRY(encode_view(&kk.own[1], a->v, pb, 128));
+  TTT_TRY(encode_view(&kk.own[2], a->uk, pb, 128));
+  TTT_TRY(encode_view(&kk.own[3], a->uv, pb, 128));
+  TTT_TRY(encode_view(&kk.str[0], a->q, pb, 64));
+  TTT_TRY(encode_view(&kk.str[1], a->dout, pb, 64));
+  TTT_TRY(encode_view(&kk.str[2], a->uq, pb, 64));
+  TTT_TRY(encode_stats(&kk.st[0], a->lse2, bh, t_pad));
+  TTT_TRY(encode_stats(&kk.st[1], a->delta, bh, t_pad));
+  TTT_TRY(encode_stats(&kk.st[2], a->gamma, bh, t_pad));
+  TTT_TRY(encode_stats(&kk.st[3], a->rho, bh, t_pad));
+  set_out0(kk, a->gk);
+  set_out1(kk, a->gv);
+  TTT_TRY(launched(ttt::launch_km(kk, pb.d, bf16, causal, ttt::kBwd2KV, s)));
+  return TTT_OK;
+}
+
+int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn_major,
+                           int32_t* err, void* stream) {
+  if (!a || !b || !c) return TTT_ERR_NULL;
+  if (dtype != TTT_F16 && dtype != TTT_BF16) return TTT_ERR_DTYPE;
+  if (!(n == 64 || n == 128 || n == 256) || !(k == 64 || k == 128)) return TTT_ERR_SHAPE;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return TTT_ERR_ALIGN;
+  CUtensorMap ta, tb;
+  ttt_problem pa{1, 1, 128, k, dtype, 0, 1.f};
+  ttt_view va{const_cast<void*>(a), 128 * k, 128 * k, k};
+  TTT_TRY(encode_view(&ta, va, pa, 128));
+  if (b_mn_major) {
+    // b is [k x n]: rows = k, row length n (encoded as "d" = n, box 64 columns x k rows)
+    ttt_problem pbm{1, 1, k, n, dtype, 0, 1.f};
+    ttt_view vb{const_cast<void*>(b), k * n, k * n, n};
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return TTT_ERR_DRIVER;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(k), 1, 1};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(n) * 2, static_cast<cuuint64_t>(n) * k * 2,
+                             static_cast<cuuint64_t>(n) * k * 2};
+    cuuint32_t box[4] = {64, static_cast<cuuint32_t>(k), 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    (void)pbm;
+    (void)vb;
+    CUresult r = fn(&tb, dtype == TTT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                    const_cast<void*>(b), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return TTT_ERR_TENSOR_MAP;
+  } else {
+    ttt_problem pbk{1, 1, n, k, dtype, 0, 1.f};
+    ttt_view vb{const_cast<void*>(b), n * k, n * k, k};
+    TTT_TRY(encode_view(&tb, vb, pbk, n));
+  }
+  return launched(ttt::launch_selftest_umma(ta, tb, c, n, k, dtype == TTT_BF16, b_mn_major != 0, err,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

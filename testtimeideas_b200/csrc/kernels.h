@@ -1,0 +1,34 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+
+namespace ttt {
+
+cudaError_t launch_fwd(const KParams& p, int d, bool bf16, bool causal, bool save_p, cudaStream_t stream);
+// Query-major passes: kind in {kBwdQ, kStats, kBwd2Q}; gdo selects dd_dO output (kBwd2Q only).
+cudaError_t launch_qm(const KParams& p, int d, bool bf16, bool causal, int kind, bool gdo, cudaStream_t stream);
+// Key-major passes: kind in {kBwdKV, kBwd2KV}.
+cudaError_t launch_km(const KParams& p, int d, bool bf16, bool causal, int kind, cudaStream_t stream);
+
+// delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t < T, 0 for T <= t < t_pad.
+struct DeltaArgs {
+  const uint16_t* o;
+  int64_t o_sb, o_sh, o_st;
+  const uint16_t* dout;
+  int64_t d_sb, d_sh, d_st;
+  float* delta;
+  int B, H, T, t_pad, D;
+  bool bf16;
+};
+cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream);
+
+// Self-test GEMM used to validate descriptor conventions: C = A B with A a
+// 128 x K tile (K-major) and B either N x K (K-major, "score" form) or K x N
+// (MN-major, "accumulate" form); inputs through the same 4-D tensor maps.
+cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, float* c, int n, int k, bool bf16,
+                                 bool b_mn_major, int* err, cudaStream_t stream);
+
+}  // namespace ttt

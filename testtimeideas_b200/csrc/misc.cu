@@ -1,0 +1,147 @@
+// Small kernels: the delta = rowsum(dO o O) preprocessing pass and a tcgen05
+// GEMM self-test that exercises the two operand layouts every attention
+// kernel uses.
+//
+// delta replaces _attn_rowsum_kernel (ttt_kernels/backward_stubs.py:184-221):
+// the reference computes sum_j P_ij (dO_i . V_j), a T x T pass with a
+// T x T x d product; since P V = O that equals dO_i . O_i, an O(T d) read.
+#include "attn_common.cuh"
+#include "kernels.h"
+
+namespace ttt {
+
+// One warp per row; lanes read D/32 consecutive elements each.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256) attn_delta_kernel(DeltaArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  const int64_t total = static_cast<int64_t>(a.B) * a.H * a.t_pad;
+  if (row >= total) return;
+  const int bh = static_cast<int>(row / a.t_pad);
+  const int t = static_cast<int>(row % a.t_pad);
+  float acc = 0.f;
+  if (t < a.T) {
+    const int b = bh / a.H, h = bh % a.H;
+    const uint16_t* o = a.o + b * a.o_sb + h * a.o_sh + static_cast<int64_t>(t) * a.o_st;
+    const uint16_t* d = a.dout + b * a.d_sb + h * a.d_sh + static_cast<int64_t>(t) * a.d_st;
+    constexpr int PER = D / 32;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int col = lane * PER + i;
+      acc += to_f32<BF16>(o[col]) * to_f32<BF16>(d[col]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  }
+  if (lane == 0) a.delta[row] = acc;
+}
+
+cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.t_pad;
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  if (a.D == 64 && !a.bf16) attn_delta_kernel<64, false><<<grid, 256, 0, stream>>>(a);
+  else if (a.D == 64 && a.bf16) attn_delta_kernel<64, true><<<grid, 256, 0, stream>>>(a);
+  else if (a.D == 128 && !a.bf16) attn_delta_kernel<128, false><<<grid, 256, 0, stream>>>(a);
+  else if (a.D == 128 && a.bf16) attn_delta_kernel<128, true><<<grid, 256, 0, stream>>>(a);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- self-test
+// C[128 x N] = A[128 x K] * B, B K-major ([N x K] rows) or MN-major ([K x N] rows).
+struct SelftestParams {
+  CUtensorMap ta, tb;
+  float* c;
+  int n, k;
+  int* err;
+};
+
+template <bool BF16, bool B_MN>
+__global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_constant__ SelftestParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;                 // PL(128, K)
+  uint8_t* sB = smem + 128 * 128 * 2;  // PL(N, K) or PL(K, N), at most 256 x 128
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 128 * 128 * 2 + 256 * 128 * 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5;
+  const int N = p.n, K = p.k;
+  if (threadIdx.x == 0) {
+    mbar_init(bars + 0, 1);
+    mbar_init(bars + 1, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  Guard g{abort_flag, p.err};
+  if (threadIdx.x == 0) {
+    const int bytes = 128 * K * 2 + N * K * 2;
+    mbar_arrive_tx(bars + 0, bytes);
+    for (int pp = 0; pp < K / 64; ++pp) tma_load_4d(sA + pp * 128 * 128, &p.ta, bars + 0, pp * 64, 0, 0, 0);
+    if (B_MN) {
+      for (int pp = 0; pp < N / 64; ++pp) tma_load_4d(sB + pp * K * 128, &p.tb, bars + 0, pp * 64, 0, 0, 0);
+    } else {
+      for (int pp = 0; pp < K / 64; ++pp) tma_load_4d(sB + pp * N * 128, &p.tb, bars + 0, pp * 64, 0, 0, 0);
+    }
+    if (mbar_wait(bars + 0, 0, g, 1)) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_f16(128, N, BF16, false, B_MN);
+      for (int kk = 0; kk < K / 16; ++kk) {
+        const uint64_t da = desc_kmajor(smem_u32(sA), 128, kk);
+        const uint64_t db = B_MN ? desc_mnmajor(smem_u32(sB), K, kk) : desc_kmajor(smem_u32(sB), N, kk);
+        umma_ss(tmem, da, db, idesc, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(bars + 1);
+    } else {
+      mbar_drain(bars + 0, 0);
+      umma_commit(bars + 1);
+    }
+  }
+  __syncwarp();
+  if (mbar_wait(bars + 1, 0, g, 2)) {
+    tc_fence_after();
+    const int r = threadIdx.x;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    for (int c0 = 0; c0 < N; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + lane_off + c0, v);
+      for (int j = 0; j < 32; ++j) p.c[r * N + c0 + j] = v[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, float* c, int n, int k, bool bf16,
+                                 bool b_mn_major, int* err, cudaStream_t stream) {
+  SelftestParams p;
+  p.ta = ta;
+  p.tb = tb;
+  p.c = c;
+  p.n = n;
+  p.k = k;
+  p.err = err;
+  const int smem = 128 * 128 * 2 + 256 * 128 * 2 + 64 + 1024;
+  auto launch = [&](auto kern) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<1, 128, smem, stream>>>(p);
+    return cudaGetLastError();
+  };
+  if (!bf16 && !b_mn_major) return launch(selftest_umma_kernel<false, false>);
+  if (!bf16 && b_mn_major) return launch(selftest_umma_kernel<false, true>);
+  if (bf16 && !b_mn_major) return launch(selftest_umma_kernel<true, false>);
+  return launch(selftest_umma_kernel<true, true>);
+}
+
+}  // namespace ttt
