@@ -1,0 +1,355 @@
+#!/usr/bin/env python
+"""Grad-grad attention step benchmark (forward + first-order backward with
+create_graph + double backward) on B200.
+
+Default workload (the metric's T=16k multi-GPU case):
+b=8 h=32 T=16384 d=128 bf16 causal, inputs, dO and probes iid N(0,1)*0.5,
+the b*h = 256 heads split into contiguous equal shards over the N ranks (no
+collective on the data path; NCCL only for the barrier and the max-over-ranks
+timing). One step, per rank:
+
+    o = triton_attention(q, k, v, causal=True)                       # forward
+    dq, dk, dv = autograd.grad(o, (q, k, v), dO, create_graph=True)  # backward
+    gq, gk, gv = autograd.grad((dq, dk, dv), (q, k, v), (u_q, u_k, u_v))  # double backward
+
+Reported (one JSON line from rank 0):
+  value     whole-job algorithmic TFLOP/s (28*T^2*d per head, x (T+1)/(2T) causal)
+            with inputs resident in HBM, device-timed with CUDA events, max over ranks;
+  e2e       the same step through the same public API with pinned host inputs
+            copied in and the second-order results copied out inside the timed region;
+  roofline  the dominant kernel's algorithmic TFLOP/s against the measured bf16 peak;
+  cpu_baseline  the reference's math path (oracle port, fp32, host cores) on a bounded sample.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4|c3|c3nc|c2]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "grad-grad attention step ms & TFLOP/s (fwd+bwd+2nd-bwd), T=16k, 1/2/4/8 B200"
+CONFIGS = {
+    "c4": dict(b=8, h=32, t=16384, d=128, dtype="bf16", causal=True, scale_in=0.5,
+               workload="BASELINE config 4: grad-grad b=8 h=32 T=16384 d=128 bf16 causal, b*h sharded over GPUs"),
+    "c3": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=True, scale_in=1.0,
+               workload="BASELINE config 3 (largest T): grad-grad b=1 h=1 T=16384 d=64 fp16 causal"),
+    "c3nc": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=False, scale_in=1.0,
+                 workload="BASELINE config 3 (largest T): grad-grad b=1 h=1 T=16384 d=64 fp16 non-causal"),
+    "c4x8": dict(b=1, h=8, t=16384, d=128, dtype="bf16", causal=True, scale_in=0.5,
+                 workload="8-head slice of BASELINE config 4 (profiling size): T=16384 d=128 bf16 causal"),
+    "c2": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5,
+               workload="BASELINE config 2 shape: grad-grad b=2 h=4 T=2048 d=128 fp16 non-causal"),
+}
+# Algorithmic flops per head, in units of T^2 d, that each kernel kind contributes
+# (each of the 14 distinct products of the grad-grad step is assigned to the
+# kernel that first computes it; recomputed products count nowhere).
+ALGO_UNITS = {"fwd": 4, "delta": 0, "bwd_kv": 6, "bwd_q": 2, "bwd2_stats": 6, "bwd2_q": 4, "bwd2_kv": 6}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def causal_factor(t: int, causal: bool) -> float:
+    return (t + 1) / (2 * t) if causal else 1.0
+
+
+def step_flops(cfg: dict, heads: int) -> float:
+    return 28.0 * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(config_name: str) -> dict:
+    """Per-kernel DRAM bytes per launch from a committed ncu capture, if any."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if not p.exists():
+        return {}
+    try:
+        return json.loads(p.read_text()).get(config_name, {})
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- the step
+def make_inputs(cfg: dict, heads: int, rank: int, device: torch.device, seed: int = 1234) -> dict:
+    dtype = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 7919 * rank)
+    shape = (1, heads, cfg["t"], cfg["d"])
+    names = ("q", "k", "v", "do", "uq", "uk", "uv")
+    return {n: (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * cfg["scale_in"]).to(dtype)
+            for n in names}
+
+
+def gradgrad_step(x: dict, causal: bool):
+    """One step through the public, reference-compatible API."""
+    from ttt_kernels import triton_attention
+    q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+    o = triton_attention(q, k, v, causal=causal)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), x["do"], create_graph=True)
+    return torch.autograd.grad((dq, dk, dv), (q, k, v), (x["uq"], x["uk"], x["uv"]))
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_baseline(cfg: dict, t_sample: int, reps: int = 1, warm: bool = True) -> dict:
+    """The reference's math path (_attention_math + autograd twice, fp32) on this
+    host's cores for one head at T=t_sample; returns TFLOP/s of that sample."""
+    from oracle import attention_oracle as orc
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = dict(cfg, t=t_sample)
+    inp = orc.seeded_inputs(1, 1, t_sample, cfg["d"], seed=99, scale_in=cfg["scale_in"])
+    names = ("q", "k", "v", "do", "uq", "uk", "uv")
+    if warm:
+        orc.math_gradgrad(*(inp[n] for n in names), causal=cfg["causal"], dtype=torch.float32)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        orc.math_gradgrad(*(inp[n] for n in names), causal=cfg["causal"], dtype=torch.float32)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": step_flops(sample, 1) / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "ms_per_sample": dt * 1e3,
+            "sample": f"one head of the workload at T={t_sample} (d={cfg['d']}, causal={cfg['causal']}), fp32 "
+                      f"math path (_attention_math + autograd twice), {reps} timed rep(s) after 1 warm-up, "
+                      f"os.cpu_count()={os.cpu_count()}"}
+
+
+def run_reference(args, cfg: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, args.cpu_t, reps=1, warm=False)
+    runs = [cpu_baseline(cfg, args.cpu_t, reps=1, warm=False) for _ in range(args.steps)]
+    base = runs[len(runs) // 2]
+    value = statistics.median(r["value"] for r in runs)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.median(r["ms_per_sample"] for r in runs),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": {"workload": cfg["workload"], "sample_t": args.cpu_t},
+            "cpu_baseline": dict(base, value=value, sample=base["sample"] + f"; median of {args.steps} samples"),
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, cfg: dict) -> None:
+    from testtimeideas_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    total_heads = cfg["b"] * cfg["h"]
+    if total_heads % world:
+        raise SystemExit(f"{total_heads} heads do not split over {world} GPUs")
+    heads = total_heads // world
+    _lib.load_library()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    x = make_inputs(cfg, heads, rank, device)
+    for _ in range(args.warmup):
+        gradgrad_step(x, cfg["causal"])
+    _lib.check_device_errors(device)
+
+    # ---- device-timed region: inputs resident in HBM
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize(device)
+    _lib.profile_collect()
+    _lib.profile_enable(True)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        gradgrad_step(x, cfg["causal"])
+    stop.record()
+    torch.cuda.synchronize(device)
+    _lib.profile_enable(False)
+    prof = _lib.profile_collect()
+    barrier()
+    clk = clocks.stop()
+    _lib.check_device_errors(device)
+    ms = max_over_ranks(start.elapsed_time(stop))
+    ms_per_step = ms / args.steps
+    value = step_flops(cfg, total_heads) / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end: pinned host inputs -> device -> step -> results back to pinned host
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    host_in = {n: torch.empty_like(t, device="cpu").pin_memory() for n, t in x.items()}
+    for n, t in x.items():
+        host_in[n].copy_(t)
+    host_out = [torch.empty_like(x["q"], device="cpu").pin_memory() for _ in range(3)]
+    dev_in = {n: torch.empty_like(t) for n, t in x.items()}
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        for n in dev_in:
+            dev_in[n].copy_(host_in[n], non_blocking=True)
+        gg = gradgrad_step(dev_in, cfg["causal"])
+        for dst, src in zip(host_out, gg):
+            dst.copy_(src, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    e2e_value = step_flops(cfg, total_heads) / (e2e_ms * 1e-3) / 1e12
+
+    # ---- roofline of the dominant kernel (per-launch CUDA-event time inside the timed region)
+    peaks, peak_src = load_peaks()
+    kern = {k: v for k, v in prof.items() if v[0] > 0}
+    dom = max(kern, key=lambda k: kern[k][1])
+    launches, dom_ms = kern[dom]
+    per_launch_ms = dom_ms / launches
+    dom_flops = ALGO_UNITS[dom] * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+    achieved = dom_flops / (per_launch_ms * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    traffic = load_traffic(args.config).get(dom)
+    roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+                "algorithmic_flops_per_launch": dom_flops, "ms_per_launch": per_launch_ms}
+
+    gpu_launches = sum(v[0] for v in prof.values())
+    kernel_ms = {k: v[1] / args.steps for k, v in kern.items()}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, args.cpu_t, reps=1)
+
+    if rank == 0:
+        dtype = cfg["dtype"]
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": {"workload": cfg["workload"], "b": cfg["b"], "h": cfg["h"], "t": cfg["t"], "d": cfg["d"],
+                       "causal": cfg["causal"], "global_heads": total_heads, "heads_per_gpu": heads,
+                       "parallelism": f"bh-shard x{world}",
+                       "l2": "inputs larger than L2 (7 tensors of %.2f GiB per GPU)" % (
+                           x["q"].numel() * x["q"].element_size() / 2 ** 30)},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms, "steps": e2e_steps,
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": gpu_launches,
+            "kernel_ms_per_step": kernel_ms,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-t", type=int, default=4096, help="T of the one-head CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

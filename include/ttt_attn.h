@@ -120,6 +120,28 @@ typedef struct {
 } ttt_bwd2_args;
 int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream);
 
+/* Kernel kinds reported by the profiling hook. */
+enum ttt_kernel_kind {
+  TTT_K_FWD = 0,         /* forward (O, lse2 [, P]) */
+  TTT_K_DELTA = 1,       /* delta = rowsum(dout o o) */
+  TTT_K_BWD_KV = 2,      /* dk, dv (key-major) */
+  TTT_K_BWD_Q = 3,       /* dq (query-major) */
+  TTT_K_BWD2_STATS = 4,  /* gamma, rho row statistics */
+  TTT_K_BWD2_Q = 5,      /* dd_q (+ dd_dout) */
+  TTT_K_BWD2_KV = 6,     /* dd_k, dd_v */
+  TTT_K_COUNT = 7
+};
+
+/* Profiling hook (no reference counterpart; the reference times whole steps
+ * with time.time(), tests/bench_gradgrad_sweep.py:31-39). While enabled, each
+ * kernel launch is bracketed by two CUDA events recorded on its stream.
+ * ttt_attn_profile_enable returns the previous setting. */
+int ttt_attn_profile_enable(int on);
+/* Waits for the recorded events, adds per-kind launch counts and elapsed
+ * milliseconds into counts[k] / total_ms[k] for k < n_kinds, and clears the
+ * record. */
+int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds);
+
 /* roundup(t, 128): the row count of every statistics array. */
 int ttt_attn_t_pad(int t);
 /* Static description of a status code. */

@@ -131,9 +131,13 @@ def test_public_api_gradgrad(mode, causal):
 
 
 def test_public_api_reference_objective():
-    """The reference benchmark's objective: loss = mean(O), s = sum mean(g^2)."""
+    """The reference benchmark's objective: loss = mean(O), s = sum mean(g^2).
+
+    Run in bf16: with fp16 the probes of this objective (~2 g / numel, about
+    1e-9 here) underflow fp16's range, so the second-order result is zero for
+    any fp16 implementation, the reference's included."""
     import ttt_kernels
-    dtype = torch.float16
+    dtype = torch.bfloat16
     inp = _cuda_inputs(1, 1, 256, 64, dtype, seed=19, scale_in=1.0)
     q, k, v = (inp[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
     out = ttt_kernels.triton_attention(q, k, v, causal=True, bwd_mode="save_p_triton_full")
@@ -144,7 +148,7 @@ def test_public_api_reference_objective():
     for name, x in zip(("gq", "gk", "gv"), gg):
         r = ref[name]
         err = orc.max_abs_err(x.float().cpu(), r) / float(r.abs().max())
-        assert err <= 2e-2, (name, err)  # grads of 1/numel-scaled losses sit near fp16's subnormal range
+        assert err <= TOL[dtype], (name, err)
 
 
 def test_dout_requires_grad_path():

@@ -55,7 +55,8 @@ class Bwd2Args(ctypes.Structure):
 
 # Every symbol include/ttt_attn.h declares.
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
-            "ttt_attn_abi_version", "ttt_attn_selftest_umma")
+            "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect")
+KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv")
 
 _lib = None
 _lib_lock = threading.Lock()
@@ -84,6 +85,10 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         lib.ttt_attn_selftest_umma.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_void_p]
+        lib.ttt_attn_profile_enable.restype = ctypes.c_int
+        lib.ttt_attn_profile_enable.argtypes = [ctypes.c_int]
+        lib.ttt_attn_profile_collect.restype = ctypes.c_int
+        lib.ttt_attn_profile_collect.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
         if path is None:
             _lib = lib
         return lib
@@ -265,3 +270,18 @@ def selftest_umma(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool) -> torch.T
     _check(lib.ttt_attn_selftest_umma(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, k, _dtype_code(a),
                                       1 if b_mn_major else 0, error_word(a.device).data_ptr(), _stream()))
     return c
+
+
+# ---------------------------------------------------------------- profiling hook
+def profile_enable(on: bool = True) -> bool:
+    """Bracket every kernel launch with CUDA events (on its stream). Returns the previous setting."""
+    return bool(load_library().ttt_attn_profile_enable(1 if on else 0))
+
+
+def profile_collect() -> dict:
+    """{kind: (launches, total_ms)} since the last collect; waits for the recorded events."""
+    n = len(KERNEL_KINDS)
+    counts = (ctypes.c_int32 * n)()
+    ms = (ctypes.c_double * n)()
+    _check(load_library().ttt_attn_profile_collect(counts, ms, n))
+    return {k: (int(counts[i]), float(ms[i])) for i, k in enumerate(KERNEL_KINDS)}

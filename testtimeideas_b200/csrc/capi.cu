@@ -5,7 +5,9 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <vector>
 
 #include "../../include/ttt_attn.h"
 #include "kernels.h"
@@ -128,6 +130,55 @@ void set_out1(KParams& k, const ttt_view& v) {
 
 int launched(cudaError_t e) { return e == cudaSuccess ? TTT_OK : TTT_ERR_LAUNCH; }
 
+// ---------------------------------------------------------------- profiling hook
+struct ProfRecord {
+  int kind;
+  int device;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof;
+std::map<int, std::vector<cudaEvent_t>> g_event_pool;  // per device
+
+cudaEvent_t take_event(int device) {
+  auto& pool = g_event_pool[device];
+  if (!pool.empty()) {
+    cudaEvent_t e = pool.back();
+    pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets one launch with events when profiling is on.
+class ProfScope {
+ public:
+  ProfScope(int kind, cudaStream_t s) : kind_(kind), s_(s) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on) return;
+    cudaGetDevice(&dev_);
+    start_ = take_event(dev_);
+    if (start_) cudaEventRecord(start_, s_);
+  }
+  ~ProfScope() {
+    if (!start_) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEvent_t stop = take_event(dev_);
+    if (!stop) return;
+    cudaEventRecord(stop, s_);
+    g_prof.push_back({kind_, dev_, start_, stop});
+  }
+
+ private:
+  int kind_;
+  cudaStream_t s_;
+  int dev_ = 0;
+  cudaEvent_t start_ = nullptr;
+};
+
 }  // namespace
 
 extern "C" {
@@ -172,6 +223,7 @@ int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
   set_out0(k, a->o);
   k.out_f0 = a->lse2;
   k.out1 = static_cast<uint16_t*>(a->p);
+  ProfScope prof(TTT_K_FWD, static_cast<cudaStream_t>(stream));
   return launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr,
                                   static_cast<cudaStream_t>(stream)));
 }
@@ -204,7 +256,10 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
   da.t_pad = t_pad;
   da.D = pb.d;
   da.bf16 = bf16;
-  TTT_TRY(launched(ttt::launch_delta(da, s)));
+  {
+    ProfScope prof(TTT_K_DELTA, s);
+    TTT_TRY(launched(ttt::launch_delta(da, s)));
+  }
 
   // dK, dV: key-major.
   {
@@ -219,6 +274,7 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad));
     set_out0(k, a->dk);
     set_out1(k, a->dv);
+    ProfScope prof(TTT_K_BWD_KV, s);
     TTT_TRY(launched(ttt::launch_km(k, pb.d, bf16, causal, ttt::kBwdKV, s)));
   }
   // dQ: query-major.
@@ -233,6 +289,7 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     k.lse2 = a->lse2;
     k.delta = a->delta;
     set_out0(k, a->dq);
+    ProfScope prof(TTT_K_BWD_Q, s);
     TTT_TRY(launched(ttt::launch_qm(k, pb.d, bf16, causal, ttt::kBwdQ, false, s)));
   }
   return TTT_OK;
@@ -269,14 +326,20 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   kq.delta = a->delta;
   kq.out_f0 = a->gamma;
   kq.out_f1 = a->rho;
-  TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kStats, false, s)));
+  {
+    ProfScope prof(TTT_K_BWD2_STATS, s);
+    TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kStats, false, s)));
+  }
   kq.gamma = a->gamma;
   kq.rho = a->rho;
   kq.out_f0 = nullptr;
   kq.out_f1 = nullptr;
   set_out0(kq, a->gq);
   if (gdo) set_out1(kq, a->gdout);
-  TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s)));
+  {
+    ProfScope prof(TTT_K_BWD2_Q, s);
+    TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s)));
+  }
 
   // Key-major: dd_k, dd_v.
   KParams kk;
@@ -295,8 +358,40 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   TTT_TRY(encode_stats(&kk.st[3], a->rho, bh, t_pad));
   set_out0(kk, a->gk);
   set_out1(kk, a->gv);
-  TTT_TRY(launched(ttt::launch_km(kk, pb.d, bf16, causal, ttt::kBwd2KV, s)));
+  {
+    ProfScope prof(TTT_K_BWD2_KV, s);
+    TTT_TRY(launched(ttt::launch_km(kk, pb.d, bf16, causal, ttt::kBwd2KV, s)));
+  }
   return TTT_OK;
+}
+
+int ttt_attn_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  const int prev = g_prof_on ? 1 : 0;
+  g_prof_on = on != 0;
+  return prev;
+}
+
+int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds) {
+  std::vector<ProfRecord> recs;
+  {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    recs.swap(g_prof);
+  }
+  int status = TTT_OK;
+  for (const ProfRecord& r : recs) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess)
+      status = TTT_ERR_LAUNCH;
+    if (r.kind >= 0 && r.kind < n_kinds) {
+      if (counts) counts[r.kind] += 1;
+      if (total_ms) total_ms[r.kind] += ms;
+    }
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_event_pool[r.device].push_back(r.start);
+    g_event_pool[r.device].push_back(r.stop);
+  }
+  return status;
 }
 
 int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn_major,
