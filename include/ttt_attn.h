@@ -150,11 +150,12 @@ const char* ttt_attn_status_string(int status);
 int ttt_attn_abi_version(void);
 
 /* Test hook (no reference counterpart): one 128 x n x k tcgen05 GEMM,
- * c[128 x n] (fp32, row-major) = a[128 x k] * b, with b given as [n x k]
- * (b_mn_major = 0) or [k x n] (b_mn_major = 1), all row-major and contiguous.
+ * c[128 x n] (fp32, row-major) = a[128 x k] * b, all row-major and contiguous.
+ * mode bit 0: b is [k x n] (MN-major operand) instead of [n x k] (K-major);
+ * mode bit 1: a is staged in tensor memory (A-from-TMEM product form).
  * n in {64, 128, 256}, k in {64, 128}. */
-int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn_major,
-                           int32_t* err, void* stream);
+int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int mode, int32_t* err,
+                           void* stream);
 
 #ifdef __cplusplus
 }

@@ -50,11 +50,12 @@ def _assert_close(x, ref, dtype, name):
 @pytest.mark.parametrize("b_mn", [False, True])
 @pytest.mark.parametrize("n", [64, 128, 256])
 @pytest.mark.parametrize("k", [64, 128])
-def test_selftest_umma(dtype, b_mn, n, k):
+@pytest.mark.parametrize("a_tmem", [False, True])
+def test_selftest_umma(dtype, b_mn, n, k, a_tmem):
     g = torch.Generator().manual_seed(n * 7 + k)
     a = torch.randn(128, k, generator=g).to(dtype).cuda()
     b = torch.randn(k, n, generator=g).to(dtype).cuda() if b_mn else torch.randn(n, k, generator=g).to(dtype).cuda()
-    c = _lib.selftest_umma(a, b, b_mn)
+    c = _lib.selftest_umma(a, b, b_mn, a_tmem)
     ref = a.float() @ (b.float() if b_mn else b.float().t())
     torch.cuda.synchronize()
     assert (c - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())

@@ -260,15 +260,17 @@ def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float
     return gq, gk, gv, gdout
 
 
-def selftest_umma(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool) -> torch.Tensor:
-    """c = a @ (b if b_mn_major else b.T) on one tcgen05 tile (test hook)."""
+def selftest_umma(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool, a_tmem: bool = False) -> torch.Tensor:
+    """c = a @ (b if b_mn_major else b.T) on one tcgen05 tile (test hook); with a_tmem the
+    A operand is staged in tensor memory."""
     lib = load_library()
     a, b = a.contiguous(), b.contiguous()
     k = a.shape[1]
     n = b.shape[1] if b_mn_major else b.shape[0]
     c = torch.empty((128, n), dtype=torch.float32, device=a.device)
     _check(lib.ttt_attn_selftest_umma(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, k, _dtype_code(a),
-                                      1 if b_mn_major else 0, error_word(a.device).data_ptr(), _stream()))
+                                      (1 if b_mn_major else 0) | (2 if a_tmem else 0),
+                                      error_word(a.device).data_ptr(), _stream()))
     return c
 
 

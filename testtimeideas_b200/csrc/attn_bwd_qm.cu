@@ -1,6 +1,6 @@
 // Query-major backward passes (sm_100a). One CTA owns 128 query rows of one
-// head and streams 64-key tiles; thread r of the four compute warps owns
-// query row r (TMEM lane r).
+// head and streams BN-key tiles (BN = 64; 32 only for the 128-wide double
+// backward that also returns dd_dO).
 //
 //   kBwdQ  : dQ = scale * dS K,  dS = P o (dP - delta),  P = 2^(S*c - lse2)
 //            (replaces _attn_bwd_dq_kernel, ttt_kernels/backward_stubs.py:259-309)
@@ -11,71 +11,104 @@
 //            A2 = sum P G_dS dP, A4 = sum P dP, A3 = sum P (dO u_v^T).
 //   kBwd2Q : dd_Q  = scale * (dS u_k + G_S K),     G_S  = P o (G_P - rho)
 //            dd_dO = G_dP V + P u_v  (GDO only),   G_dP = P o (G_dS - gamma)
-//            (together with the key-major kBwd2KV pass this replaces the
-//            PyTorch matmul double backward of TritonDvFn / TritonRowSumFn /
-//            TritonDqDkFn, backward_stubs.py:435-514, with the complete
-//            second-order terms)
+//            (with the key-major kBwd2KV pass this replaces the PyTorch matmul
+//            double backward of TritonDvFn / TritonRowSumFn / TritonDqDkFn,
+//            backward_stubs.py:435-514, with the complete second-order terms)
 //
-// Roles: warp 5 = TMA producer, warp 4 = MMA issuer (one thread), warps 0..3 =
-// elementwise. Score tiles (S, dP, G_dS, dO u_v^T) land in TMEM; the
-// elementwise results that feed the second GEMM (dS, G_S, G_dP, P) go to
-// shared memory in the 128-byte-swizzled K-major layout; accumulators stay in
-// TMEM until the epilogue. Causal: key tiles past the diagonal are skipped.
-#include "attn_common.cuh"
+// Roles (320 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
+// thread), warp 9 TMA producer. Compute warp w owns TMEM lanes 32*(w%4)..+31
+// (one query row per thread) and columns (w/4)*BN/2 .. +BN/2 of every tile.
+//
+// Score products that share their A operand run as one N = 2*BN product: the
+// streamed K and u_k tiles sit stacked in one panel ([K; u_k]), as do V and
+// u_v, so Q [K; u_k]^T yields [S | Q u_k^T] and dO [V; u_v]^T yields
+// [dP | dO u_v^T]; u_q K^T then accumulates into the second half of the first.
+// (On B200 an M=128 UMMA with N <= 64 costs about as much as one with N=128.)
+//
+// Pipeline per tile n: tile n's score products are issued as soon as the
+// compute warps have read the previous contents of that TMEM buffer (s_free);
+// tile n-1's accumulate products once its elementwise results are in shared
+// memory (e_full). Streamed tiles use a 2..4-stage TMA ring sized from the
+// shared-memory budget. For the 128-wide double backward the elementwise
+// results are written into the [V; u_v] part of their own stage, which only the
+// score products read. Causal: key tiles past the diagonal are skipped and only
+// boundary tiles are masked.
+#include "attn_pipe.cuh"
 #include "kernels.h"
 
 namespace ttt {
 
 template <int D, int KIND, bool GDO>
 struct QmCfg {
-  static constexpr int BM = 128, BN = 64;
+  static constexpr int BM = 128;
   static constexpr bool BWD2 = (KIND != kBwdQ);
+  static constexpr int BN = (D == 128 && KIND == kBwd2Q && GDO) ? 32 : 64;
   static constexpr int NR = BWD2 ? 3 : 2;    // resident: Q, dO, (u_q)
-  static constexpr int NSTR = BWD2 ? 4 : 2;  // streamed: K, V, (u_k, u_v)
-  static constexpr int NSC = BWD2 ? 4 : 2;   // score tiles: S, dP, (G_dS, dO u_v^T)
+  static constexpr int NSC = BWD2 ? 4 : 2;   // score tiles: S, (G_dS,) dP, (dO u_v^T)
   static constexpr int NE = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 4 : 2));
   static constexpr int NA = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 2 : 1));
+  static constexpr int NCW = 8;
+  static constexpr int NCT = NCW * 32;
+  static constexpr int NTHREADS = NCT + 64;
+  static constexpr int CPW = BN / 2;
+  // streamed tiles: ST0 = [K; u_k] (or K), ST1 = [V; u_v] (or V), rows stacked per panel
+  static constexpr int ST_ROWS = BWD2 ? 2 * BN : BN;
+  static constexpr int ST_BYTES = ST_ROWS * D * 2;
+  static constexpr int STAGE = 2 * ST_BYTES;
   static constexpr int TILE_R = BM * D * 2;
-  static constexpr int TILE_S = BN * D * 2;
-  static constexpr int TILE_E = BM * BN * 2;
+  static constexpr int TILE_E = BM * 64 * 2;  // one 64-column panel (BN <= 64 columns used)
+  // elementwise results in the ST1 part of their own stage when they fit
+  static constexpr bool EIS = (KIND == kBwd2Q) && (NE * TILE_E <= ST_BYTES);
+  static constexpr int E_BYTES = EIS ? 0 : NE * TILE_E;
   static constexpr int NBUF = (2 * NSC * BN + NA * D <= 512) ? 2 : 1;
   static constexpr int TMEM_USED = NBUF * NSC * BN + NA * D;
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
-  static constexpr int FIXED = NR * TILE_R + NBUF * NE * TILE_E;
-  static constexpr int NSTAGE = (FIXED + 2 * NSTR * TILE_S + 2048 <= 232448) ? 2 : 1;
+  static constexpr int FIXED = NR * TILE_R + E_BYTES + 16 * 8 + 16 + 1024;
+  static constexpr int NSTAGE = (FIXED + 4 * STAGE <= 232448) ? 4 : (FIXED + 3 * STAGE <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
   static constexpr int OFF_S = OFF_R + NR * TILE_R;
-  static constexpr int OFF_E = OFF_S + NSTAGE * NSTR * TILE_S;
-  static constexpr int OFF_BAR = OFF_E + NBUF * NE * TILE_E;
+  static constexpr int OFF_E = OFF_S + NSTAGE * STAGE;
+  static constexpr int OFF_BAR = OFF_E + E_BYTES;
   static constexpr int NBAR = 16;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "query-major tile set exceeds shared memory");
+  // TMEM column offsets of the score tiles within one buffer
+  static constexpr int C_S = 0, C_GDS = BWD2 ? BN : 0, C_DP = BWD2 ? 2 * BN : BN, C_UV = 3 * BN;
 };
 
+int qm_tile_cols(int d, int kind, bool gdo) { return (d == 128 && kind == kBwd2Q && gdo) ? 32 : 64; }
+
 template <int D, bool BF16, bool CAUSAL, int KIND, bool GDO>
-__global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__ KParams p) {
+__global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kernel(const __grid_constant__ KParams p) {
   using C = QmCfg<D, KIND, GDO>;
-  constexpr int BM = C::BM, BN = C::BN, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE;
+  constexpr int BM = C::BM, BN = C::BN, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE, CPW = C::CPW;
+  constexpr int SR = C::ST_ROWS;
+  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sR = smem + C::OFF_R;
   uint8_t* sS = smem + C::OFF_S;
   uint8_t* sE = smem + C::OFF_E;
+  // Row-sum scratch of the stats pass: reuses the streamed-tile stages, which
+  // are idle once every compute thread has seen the last tile's scores land.
+  float* red = reinterpret_cast<float*>(smem + C::OFF_S);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
-  uint64_t* l_full = bars + 1;   // [2]
-  uint64_t* l_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;   // [2]
-  uint64_t* e_full = bars + 7;   // [2] (128 arrivals)
-  uint64_t* e_empty = bars + 9;  // [2]
-  uint64_t* acc_full = bars + 11;
-  uint64_t* drain = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  uint64_t* l_full = bars + 1;   // [4] TMA -> MMA
+  uint64_t* l_empty = bars + 5;  // [4] MMA -> TMA
+  uint64_t* s_full = bars + 9;   // [2] MMA -> compute
+  uint64_t* s_free = bars + 11;  // [2] compute -> MMA (NCT arrivals)
+  uint64_t* e_full = bars + 13;  // compute -> MMA (NCT arrivals)
+  uint64_t* e_empty = bars + 14; // MMA -> compute
+  uint64_t* acc_full = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  static_assert(17 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
   auto tileR = [&](int t) { return sR + t * C::TILE_R; };
-  auto tileS = [&](int s, int t) { return sS + (s * C::NSTR + t) * C::TILE_S; };
-  auto tileE = [&](int b, int t) { return sE + (b * C::NE + t) * C::TILE_E; };
+  auto tileS = [&](int s, int t) { return sS + s * C::STAGE + t * C::ST_BYTES; };
+  auto tileE = [&](int s, int t) { return C::EIS ? tileS(s, 1) + t * C::TILE_E : sE + t * C::TILE_E; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -87,9 +120,10 @@ __global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__
   const int n_tiles = CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 13; ++i) mbar_init(bars + i, 1);
-    mbar_init(e_full + 0, 128);
-    mbar_init(e_full + 1, 128);
+    for (int i = 0; i < 17; ++i) mbar_init(bars + i, 1);
+    mbar_init(s_free + 0, C::NCT);
+    mbar_init(s_free + 1, C::NCT);
+    mbar_init(e_full, C::NCT);
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
     fence_mbar_init();
@@ -108,12 +142,13 @@ __global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__
   const uint32_t tAcc1 = tAcc0 + D;
   Guard g{abort_flag, p.err};
 
-  if (warp == 5) {
+  if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      constexpr int NSTR = C::BWD2 ? 4 : 2;
       for (int t = 0; t < C::NR; ++t) tma_prefetch(&p.own[t]);
-      for (int t = 0; t < C::NSTR; ++t) tma_prefetch(&p.str[t]);
-      int issued[2] = {0, 0};
+      for (int t = 0; t < NSTR; ++t) tma_prefetch(&p.str[t]);
+      int issued[4] = {0, 0, 0, 0};
       mbar_arrive_tx(res_full, C::NR * C::TILE_R);
       for (int t = 0; t < C::NR; ++t)
         for (int pp = 0; pp < NP; ++pp)
@@ -121,111 +156,112 @@ __global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__
       for (int n = 0; n < n_tiles; ++n) {
         const int s = n % NSTAGE;
         if (n >= NSTAGE && !mbar_wait(l_empty + s, ((n / NSTAGE) - 1) & 1, g, 1)) break;
-        mbar_arrive_tx(l_full + s, C::NSTR * C::TILE_S);
-        for (int t = 0; t < C::NSTR; ++t)
+        mbar_arrive_tx(l_full + s, NSTR * BN * D * 2);
+        // str[0] = K, str[1] = V, str[2] = u_k, str[3] = u_v
+        for (int t = 0; t < NSTR; ++t) {
+          uint8_t* dst = tileS(s, t & 1) + (t >> 1) * BN * 128;
           for (int pp = 0; pp < NP; ++pp)
-            tma_load_4d(tileS(s, t) + pp * BN * 128, &p.str[t], l_full + s, pp * 64, n * BN, hidx, bidx);
+            tma_load_4d(dst + pp * SR * 128, &p.str[t], l_full + s, pp * 64, n * BN, hidx, bidx);
+        }
         issued[s] = n + 1;
       }
       mbar_drain(res_full, 0);
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-  } else if (warp == 4) {
+  } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t id_sc = idesc_f16(128, BN, BF16, false, false);
+      constexpr uint32_t id_n1 = idesc_f16(128, BN, BF16, false, false);
+      constexpr uint32_t id_n2 = idesc_f16(128, 2 * BN, BF16, false, false);
       constexpr uint32_t id_acc = idesc_f16(128, D, BF16, false, true);
       const uint32_t aQ = smem_u32(tileR(0)), aDO = smem_u32(tileR(1));
       const uint32_t aUQ = C::BWD2 ? smem_u32(tileR(2)) : 0u;
       auto issue_scores = [&](int n) -> bool {
         const int sb = n % NBUF, s = n % NSTAGE;
         if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2)) return false;
+        if (n >= NBUF && !mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3)) return false;
         tc_fence_after();
         const uint32_t base = tmem + sb * C::NSC * BN;
-        const uint32_t bK = smem_u32(tileS(s, 0)), bV = smem_u32(tileS(s, 1));
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(base, desc_kmajor(aQ, BM, kk), desc_kmajor(bK, BN, kk), id_sc, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(base + BN, desc_kmajor(aDO, BM, kk), desc_kmajor(bV, BN, kk), id_sc, kk > 0);
+        const uint32_t b0 = smem_u32(tileS(s, 0)), b1 = smem_u32(tileS(s, 1));
         if constexpr (C::BWD2) {
-          const uint32_t bUK = smem_u32(tileS(s, 2)), bUV = smem_u32(tileS(s, 3));
+          // [S | Q u_k^T] = Q [K; u_k]^T ; G_dS/scale += u_q K^T ; [dP | dO u_v^T] = dO [V; u_v]^T
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + 2 * BN, desc_kmajor(aUQ, BM, kk), desc_kmajor(bK, BN, kk), id_sc, kk > 0);
+            umma_ss(base + C::C_S, desc_kmajor(aQ, BM, kk), desc_kmajor(b0, SR, kk), id_n2, kk > 0);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + 2 * BN, desc_kmajor(aQ, BM, kk), desc_kmajor(bUK, BN, kk), id_sc, 1u);
+            umma_ss(base + C::C_GDS, desc_kmajor(aUQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, 1u);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + 3 * BN, desc_kmajor(aDO, BM, kk), desc_kmajor(bUV, BN, kk), id_sc, kk > 0);
+            umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n2, kk > 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss(base + C::C_S, desc_kmajor(aQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n1, kk > 0);
         }
         umma_commit(s_full + sb);
         if constexpr (C::NA == 0) umma_commit(l_empty + s);
         return true;
       };
       auto issue_acc = [&](int n) -> bool {
-        const int sb = n % NBUF, s = n % NSTAGE;
-        if (!mbar_wait(e_full + sb, (n / NBUF) & 1, g, 3)) return false;
+        const int s = n % NSTAGE;
+        if (!mbar_wait(e_full, n & 1, g, 4)) return false;
         tc_fence_after();
         const uint32_t bK = smem_u32(tileS(s, 0)), bV = smem_u32(tileS(s, 1));
-        const uint32_t e0 = smem_u32(tileE(sb, 0));
+        const uint32_t e0 = smem_u32(tileE(s, 0));
         if constexpr (KIND == kBwdQ) {
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bK, BN, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+            umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bK, SR, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
         } else {
-          const uint32_t bUK = smem_u32(tileS(s, 2)), bUV = smem_u32(tileS(s, 3));
-          const uint32_t e1 = smem_u32(tileE(sb, 1));
+          const uint32_t bUK = bK + BN * 128, bUV = bV + BN * 128;
+          const uint32_t e1 = smem_u32(tileE(s, 1));
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bUK, BN, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+            umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bUK, SR, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e1, BM, kk), desc_mnmajor(bK, BN, kk), id_acc, 1u);
+            umma_ss(tAcc0, desc_kmajor(e1, BM, kk), desc_mnmajor(bK, SR, kk), id_acc, 1u);
           if constexpr (GDO) {
-            const uint32_t e2 = smem_u32(tileE(sb, 2)), e3 = smem_u32(tileE(sb, 3));
+            const uint32_t e2 = smem_u32(tileE(s, 2)), e3 = smem_u32(tileE(s, 3));
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk)
-              umma_ss(tAcc1, desc_kmajor(e2, BM, kk), desc_mnmajor(bV, BN, kk), id_acc,
+              umma_ss(tAcc1, desc_kmajor(e2, BM, kk), desc_mnmajor(bV, SR, kk), id_acc,
                       (n > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk)
-              umma_ss(tAcc1, desc_kmajor(e3, BM, kk), desc_mnmajor(bUV, BN, kk), id_acc, 1u);
+              umma_ss(tAcc1, desc_kmajor(e3, BM, kk), desc_mnmajor(bUV, SR, kk), id_acc, 1u);
           }
         }
-        umma_commit(e_empty + sb);
+        if constexpr (!C::EIS) umma_commit(e_empty);
         umma_commit(l_empty + s);
         return true;
       };
-      constexpr int LA = NBUF - 1;
-      bool ok = mbar_wait(res_full, 0, g, 4);
-      for (int n = 0; ok && n < LA && n < n_tiles; ++n) ok = issue_scores(n);
+      bool ok = mbar_wait(res_full, 0, g, 1);
       for (int n = 0; ok && n < n_tiles; ++n) {
-        const int m = n + LA;
-        if (m < n_tiles) {
-          if constexpr (C::NA == 0) {
-            if (m >= NBUF && !mbar_wait(e_full + (m % NBUF), ((m / NBUF) - 1) & 1, g, 5)) { ok = false; break; }
-          }
-          if (!issue_scores(m)) { ok = false; break; }
-        }
+        ok = issue_scores(n);
         if constexpr (C::NA > 0) {
-          if (!issue_acc(n)) { ok = false; break; }
+          if (ok && n >= 1) ok = issue_acc(n - 1);
         }
       }
       if constexpr (C::NA > 0) {
+        if (ok) ok = issue_acc(n_tiles - 1);
         if (ok) umma_commit(acc_full);
       }
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
   } else {
-    // ------------------------------------------------------------ elementwise warps 0..3
-    const int r = threadIdx.x;
+    // ------------------------------------------------------------ elementwise warps 0..7
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int row = q0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int c0 = half * CPW;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int64_t sidx = static_cast<int64_t>(bh) * p.t_pad + row;
     const float c = p.scale_log2, scale = p.scale;
     const float lse = p.lse2[sidx];
@@ -238,65 +274,87 @@ __global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__
     float a_g = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
-      const int sb = n % NBUF;
+      const int sb = n % NBUF, s = n % NSTAGE;
       if (!mbar_wait(s_full + sb, (n / NBUF) & 1, g, 6)) { ok = false; break; }
       tc_fence_after();
-      if constexpr (C::NE > 0) {
-        if (n >= NBUF && !mbar_wait(e_empty + sb, ((n / NBUF) - 1) & 1, g, 7)) { ok = false; break; }
+      const uint32_t base = tmem + lane_off + sb * C::NSC * BN + c0;
+      float sv[CPW], dp[CPW], gd[CPW], uv[CPW];
+      tmem_ld_nw<CPW>(base + C::C_S, sv);
+      tmem_ld_nw<CPW>(base + C::C_DP, dp);
+      if constexpr (C::BWD2) {
+        tmem_ld_nw<CPW>(base + C::C_GDS, gd);
+        tmem_ld_nw<CPW>(base + C::C_UV, uv);
       }
-      const uint32_t base = tmem + lane_off + sb * C::NSC * BN;
+      tmem_wait_ld();
+      reg_fence(sv);
+      reg_fence(dp);
+      if constexpr (C::BWD2) {
+        reg_fence(gd);
+        reg_fence(uv);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free + sb);  // scores are in registers: the next tile's products may overwrite them
+
+      const int j0 = n * BN + c0;
+      const bool need_mask = (n * BN + BN > T) || (CAUSAL && n * BN + BN - 1 > q0);
 #pragma unroll
-      for (int half = 0; half < BN / 32; ++half) {
-        const int cc = half * 32;
-        float sv[32], dp[32], gd[32], uv[32];
-        tmem_ld32(base + cc, sv);
-        tmem_ld32(base + BN + cc, dp);
-        if constexpr (C::BWD2) {
-          tmem_ld32(base + 2 * BN + cc, gd);
-          tmem_ld32(base + 3 * BN + cc, uv);
-        }
-        const int j0 = n * BN + cc;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
+      for (int e = 0; e < CPW; ++e) {
+        float pr = fast_exp2(fmaf(sv[e], c, -lse));
+        if (need_mask) {
           const int j = j0 + e;
-          const bool valid = (j < T) && (!CAUSAL || j <= row);
-          const float pr = valid ? fast_exp2(sv[e] * c - lse) : 0.f;
-          if constexpr (KIND == kBwdQ) {
-            sv[e] = pr * (dp[e] - del);
-          } else if constexpr (KIND == kStats) {
-            const float t = pr * (gd[e] * scale);
-            a_g += t;
-            a2 += t * dp[e];
-            a4 += pr * dp[e];
-            a3 += pr * uv[e];
-          } else {
-            const float dpm = dp[e] - del;
-            const float gds = gd[e] * scale;
-            const float gP = gds * dpm - gam * dp[e] + uv[e];
-            sv[e] = pr * dpm;          // dS
-            dp[e] = pr * (gP - rho);   // G_S
-            gd[e] = pr * (gds - gam);  // G_dP
-            uv[e] = pr;                // P
-          }
+          pr = ((j < T) && (!CAUSAL || j <= row)) ? pr : 0.f;
         }
         if constexpr (KIND == kBwdQ) {
-          store_row32<BF16>(tileE(sb, 0), BM, r, cc, sv);
-        } else if constexpr (KIND == kBwd2Q) {
-          store_row32<BF16>(tileE(sb, 0), BM, r, cc, sv);
-          store_row32<BF16>(tileE(sb, 1), BM, r, cc, dp);
-          if constexpr (GDO) {
-            store_row32<BF16>(tileE(sb, 2), BM, r, cc, gd);
-            store_row32<BF16>(tileE(sb, 3), BM, r, cc, uv);
-          }
+          sv[e] = pr * (dp[e] - del);
+        } else if constexpr (KIND == kStats) {
+          const float t = pr * (gd[e] * scale);
+          a_g += t;
+          a2 = fmaf(t, dp[e], a2);
+          a4 = fmaf(pr, dp[e], a4);
+          a3 = fmaf(pr, uv[e], a3);
+        } else {
+          const float dpm = dp[e] - del;
+          const float gds = gd[e] * scale;
+          const float gP = fmaf(gds, dpm, fmaf(-gam, dp[e], uv[e]));
+          sv[e] = pr * dpm;          // dS
+          dp[e] = pr * (gP - rho);   // G_S
+          gd[e] = pr * (gds - gam);  // G_dP
+          uv[e] = pr;                // P
         }
       }
-      if constexpr (C::NE > 0) fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(e_full + sb);
+      if constexpr (C::NE > 0) {
+        // With EIS the results go into this tile's own stage (its score
+        // products are complete), so no wait for the previous tile is needed.
+        if constexpr (!C::EIS) {
+          if (n >= 1 && !mbar_wait(e_empty, (n - 1) & 1, g, 7)) { ok = false; break; }
+        }
+        store_cols<BF16, CPW>(tileE(s, 0), BM, r, c0, sv);
+        if constexpr (KIND == kBwd2Q) {
+          store_cols<BF16, CPW>(tileE(s, 1), BM, r, c0, dp);
+          if constexpr (GDO) {
+            store_cols<BF16, CPW>(tileE(s, 2), BM, r, c0, gd);
+            store_cols<BF16, CPW>(tileE(s, 3), BM, r, c0, uv);
+          }
+        }
+        fence_async_smem();
+        mbar_arrive(e_full);
+      }
     }
     const bool valid = row < T;
     if constexpr (KIND == kStats) {
-      if (ok) {
+      // the two column halves of each row combine through shared memory
+      if (half == 1) {
+        red[r * 4 + 0] = a_g;
+        red[r * 4 + 1] = a2;
+        red[r * 4 + 2] = a3;
+        red[r * 4 + 3] = a4;
+      }
+      compute_bar<C::NCT>();
+      if (half == 0 && ok && !*abort_flag) {
+        a_g += red[r * 4 + 0];
+        a2 += red[r * 4 + 1];
+        a3 += red[r * 4 + 2];
+        a4 += red[r * 4 + 3];
         const float rho_v = a2 - del * a_g - a_g * a4 + a3;
         p.out_f0[sidx] = valid ? a_g : 0.f;
         p.out_f1[sidx] = valid ? rho_v : 0.f;
@@ -306,11 +364,11 @@ __global__ void __launch_bounds__(192, 1) attn_qm_kernel(const __grid_constant__
         tc_fence_after();
         uint16_t* r0 = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
                        static_cast<int64_t>(row) * p.o0_st;
-        acc_to_global<D, BF16>(tAcc0 + lane_off, r0, valid, scale);
+        acc_cols_to_global<D / 2, BF16>(tAcc0 + lane_off, half * (D / 2), r0, valid, scale);
         if constexpr (KIND == kBwd2Q && GDO) {
           uint16_t* r1 = p.out1 + static_cast<int64_t>(bidx) * p.o1_sb + static_cast<int64_t>(hidx) * p.o1_sh +
                          static_cast<int64_t>(row) * p.o1_st;
-          acc_to_global<D, BF16>(tAcc1 + lane_off, r1, valid, 1.f);
+          acc_cols_to_global<D / 2, BF16>(tAcc1 + lane_off, half * (D / 2), r1, valid, 1.f);
         }
       }
     }
@@ -329,7 +387,7 @@ static cudaError_t launch_qm_t(const KParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, (p.T + C::BM - 1) / C::BM);
-  kern<<<grid, 192, C::SMEM, stream>>>(p);
+  kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,92 @@
+// Helpers shared by the pipelined backward kernels: batched TMEM loads with a
+// single wait, column-slice stores into the swizzled shared-memory tiles, and
+// the named barrier of the compute warps.
+#pragma once
+
+#include "attn_common.cuh"
+
+namespace ttt {
+
+// Issue a 16- or 32-column TMEM load without waiting; call tmem_wait_ld()
+// and reg_fence() before reading the registers.
+TTT_DEV void tmem_ld16_nw(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+TTT_DEV void tmem_ld32_nw(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+template <int W>
+TTT_DEV void tmem_ld_nw(uint32_t taddr, float (&v)[W]) {
+  static_assert(W == 16 || W == 32, "");
+  if constexpr (W == 16) tmem_ld16_nw(taddr, v);
+  else tmem_ld32_nw(taddr, v);
+}
+
+TTT_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Orders the reads of registers filled by an asynchronous TMEM load after the
+// preceding tcgen05.wait::ld (volatile asm statements keep their order).
+template <int N>
+TTT_DEV void reg_fence(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
+
+// Write W (16 or 32) consecutive values of row r, columns c0 .. c0+W-1 (c0 a
+// multiple of W inside one 64-column panel), into a PL(R, C) tile.
+template <bool BF16, int W>
+TTT_DEV void store_cols(uint8_t* tile, int R, int r, int c0, const float* v) {
+  uint8_t* rowp = tile + (c0 >> 6) * R * 128 + r * 128;
+  const int ch0 = (c0 & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < W / 8; ++q) {
+    uint4 w;
+    w.x = pack2<BF16>(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack2<BF16>(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack2<BF16>(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack2<BF16>(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(rowp + (((ch0 + q) ^ (r & 7)) << 4)) = w;
+  }
+}
+
+// Named barrier 1 over the compute warps only (the producer and MMA warps
+// never take part).
+template <int NTHREADS>
+TTT_DEV void compute_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NTHREADS) : "memory");
+}
+
+// Copy `ncols` accumulator columns starting at col0 (a multiple of 32) of a
+// TMEM row to a 16-bit global row, scaled by `mul`; warp-collective.
+template <int NCOLS, bool BF16>
+TTT_DEV void acc_cols_to_global(uint32_t taddr_row, int col0, uint16_t* dst_row, bool valid, float mul) {
+#pragma unroll
+  for (int c = 0; c < NCOLS / 32; ++c) {
+    float v[32];
+    tmem_ld32(taddr_row + col0 + c * 32, v);
+    if (valid) store_global32<BF16>(dst_row + col0 + c * 32, v, mul);
+  }
+}
+
+}  // namespace ttt

@@ -9,7 +9,7 @@
 #include <mutex>
 #include <vector>
 
-#include "../../include/ttt_attn.h"
+#include "ttt_attn.h"
 #include "kernels.h"
 
 namespace {
@@ -85,13 +85,13 @@ int encode_view(CUtensorMap* m, const ttt_view& v, const ttt_problem& pb, int ro
   return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
 }
 
-// 2-D map over fp32 statistics [bh, t_pad], box (64, 1).
-int encode_stats(CUtensorMap* m, const float* p, int bh, int t_pad) {
+// 2-D map over fp32 statistics [bh, t_pad], box (cols, 1).
+int encode_stats(CUtensorMap* m, const float* p, int bh, int t_pad, int cols) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return TTT_ERR_DRIVER;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(t_pad), static_cast<cuuint64_t>(bh)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(t_pad) * 4};
-  cuuint32_t box[2] = {64, 1};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(cols), 1};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -268,10 +268,11 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     fill_common(k, pb, a->err);
     TTT_TRY(encode_view(&k.own[0], a->k, pb, 128));
     TTT_TRY(encode_view(&k.own[1], a->v, pb, 128));
-    TTT_TRY(encode_view(&k.str[0], a->q, pb, 64));
-    TTT_TRY(encode_view(&k.str[1], a->dout, pb, 64));
-    TTT_TRY(encode_stats(&k.st[0], a->lse2, bh, t_pad));
-    TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad));
+    const int rows = ttt::km_tile_rows(pb.d, ttt::kBwdKV);
+    TTT_TRY(encode_view(&k.str[0], a->q, pb, rows));
+    TTT_TRY(encode_view(&k.str[1], a->dout, pb, rows));
+    TTT_TRY(encode_stats(&k.st[0], a->lse2, bh, t_pad, rows));
+    TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad, rows));
     set_out0(k, a->dk);
     set_out1(k, a->dv);
     ProfScope prof(TTT_K_BWD_KV, s);
@@ -284,8 +285,9 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     fill_common(k, pb, a->err);
     TTT_TRY(encode_view(&k.own[0], a->q, pb, 128));
     TTT_TRY(encode_view(&k.own[1], a->dout, pb, 128));
-    TTT_TRY(encode_view(&k.str[0], a->k, pb, 64));
-    TTT_TRY(encode_view(&k.str[1], a->v, pb, 64));
+    const int cols = ttt::qm_tile_cols(pb.d, ttt::kBwdQ, false);
+    TTT_TRY(encode_view(&k.str[0], a->k, pb, cols));
+    TTT_TRY(encode_view(&k.str[1], a->v, pb, cols));
     k.lse2 = a->lse2;
     k.delta = a->delta;
     set_out0(k, a->dq);
@@ -318,10 +320,14 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   TTT_TRY(encode_view(&kq.own[0], a->q, pb, 128));
   TTT_TRY(encode_view(&kq.own[1], a->dout, pb, 128));
   TTT_TRY(encode_view(&kq.own[2], a->uq, pb, 128));
-  TTT_TRY(encode_view(&kq.str[0], a->k, pb, 64));
-  TTT_TRY(encode_view(&kq.str[1], a->v, pb, 64));
-  TTT_TRY(encode_view(&kq.str[2], a->uk, pb, 64));
-  TTT_TRY(encode_view(&kq.str[3], a->uv, pb, 64));
+  auto encode_stream_q = [&](int cols) -> int {
+    TTT_TRY(encode_view(&kq.str[0], a->k, pb, cols));
+    TTT_TRY(encode_view(&kq.str[1], a->v, pb, cols));
+    TTT_TRY(encode_view(&kq.str[2], a->uk, pb, cols));
+    TTT_TRY(encode_view(&kq.str[3], a->uv, pb, cols));
+    return TTT_OK;
+  };
+  TTT_TRY(encode_stream_q(ttt::qm_tile_cols(pb.d, ttt::kStats, false)));
   kq.lse2 = a->lse2;
   kq.delta = a->delta;
   kq.out_f0 = a->gamma;
@@ -330,6 +336,8 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
     ProfScope prof(TTT_K_BWD2_STATS, s);
     TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kStats, false, s)));
   }
+  if (ttt::qm_tile_cols(pb.d, ttt::kBwd2Q, gdo) != ttt::qm_tile_cols(pb.d, ttt::kStats, false))
+    TTT_TRY(encode_stream_q(ttt::qm_tile_cols(pb.d, ttt::kBwd2Q, gdo)));
   kq.gamma = a->gamma;
   kq.rho = a->rho;
   kq.out_f0 = nullptr;
@@ -349,13 +357,14 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   TTT_TRY(encode_view(&kk.own[1], a->v, pb, 128));
   TTT_TRY(encode_view(&kk.own[2], a->uk, pb, 128));
   TTT_TRY(encode_view(&kk.own[3], a->uv, pb, 128));
-  TTT_TRY(encode_view(&kk.str[0], a->q, pb, 64));
-  TTT_TRY(encode_view(&kk.str[1], a->dout, pb, 64));
-  TTT_TRY(encode_view(&kk.str[2], a->uq, pb, 64));
-  TTT_TRY(encode_stats(&kk.st[0], a->lse2, bh, t_pad));
-  TTT_TRY(encode_stats(&kk.st[1], a->delta, bh, t_pad));
-  TTT_TRY(encode_stats(&kk.st[2], a->gamma, bh, t_pad));
-  TTT_TRY(encode_stats(&kk.st[3], a->rho, bh, t_pad));
+  const int rows = ttt::km_tile_rows(pb.d, ttt::kBwd2KV);
+  TTT_TRY(encode_view(&kk.str[0], a->q, pb, rows));
+  TTT_TRY(encode_view(&kk.str[1], a->dout, pb, rows));
+  TTT_TRY(encode_view(&kk.str[2], a->uq, pb, rows));
+  TTT_TRY(encode_stats(&kk.st[0], a->lse2, bh, t_pad, rows));
+  TTT_TRY(encode_stats(&kk.st[1], a->delta, bh, t_pad, rows));
+  TTT_TRY(encode_stats(&kk.st[2], a->gamma, bh, t_pad, rows));
+  TTT_TRY(encode_stats(&kk.st[3], a->rho, bh, t_pad, rows));
   set_out0(kk, a->gk);
   set_out1(kk, a->gv);
   {
@@ -394,8 +403,10 @@ int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds) {
   return status;
 }
 
-int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int b_mn_major,
-                           int32_t* err, void* stream) {
+int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int mode, int32_t* err,
+                           void* stream) {
+  const int b_mn_major = mode & 1;
+  const bool a_tmem = (mode & 2) != 0;
   if (!a || !b || !c) return TTT_ERR_NULL;
   if (dtype != TTT_F16 && dtype != TTT_BF16) return TTT_ERR_DTYPE;
   if (!(n == 64 || n == 128 || n == 256) || !(k == 64 || k == 128)) return TTT_ERR_SHAPE;
@@ -406,8 +417,6 @@ int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k,
   TTT_TRY(encode_view(&ta, va, pa, 128));
   if (b_mn_major) {
     // b is [k x n]: rows = k, row length n (encoded as "d" = n, box 64 columns x k rows)
-    ttt_problem pbm{1, 1, k, n, dtype, 0, 1.f};
-    ttt_view vb{const_cast<void*>(b), k * n, k * n, n};
     EncodeTiledFn fn = encode_fn();
     if (!fn) return TTT_ERR_DRIVER;
     cuuint64_t dims[4] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(k), 1, 1};
@@ -415,8 +424,6 @@ int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k,
                              static_cast<cuuint64_t>(n) * k * 2};
     cuuint32_t box[4] = {64, static_cast<cuuint32_t>(k), 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    (void)pbm;
-    (void)vb;
     CUresult r = fn(&tb, dtype == TTT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                     const_cast<void*>(b), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -426,7 +433,7 @@ int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k,
     ttt_view vb{const_cast<void*>(b), n * k, n * k, k};
     TTT_TRY(encode_view(&tb, vb, pbk, n));
   }
-  return launched(ttt::launch_selftest_umma(ta, tb, c, n, k, dtype == TTT_BF16, b_mn_major != 0, err,
+  return launched(ttt::launch_selftest_umma(ta, tb, a, c, n, k, dtype == TTT_BF16, b_mn_major != 0, a_tmem, err,
                                             static_cast<cudaStream_t>(stream)));
 }
 

@@ -12,6 +12,10 @@ cudaError_t launch_fwd(const KParams& p, int d, bool bf16, bool causal, bool sav
 cudaError_t launch_qm(const KParams& p, int d, bool bf16, bool causal, int kind, bool gdo, cudaStream_t stream);
 // Key-major passes: kind in {kBwdKV, kBwd2KV}.
 cudaError_t launch_km(const KParams& p, int d, bool bf16, bool causal, int kind, cudaStream_t stream);
+// Rows of the streamed tiles (and of the per-query statistics boxes) each pass
+// expects in its tensor maps.
+int qm_tile_cols(int d, int kind, bool gdo);
+int km_tile_rows(int d, int kind);
 
 // delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t < T, 0 for T <= t < t_pad.
 struct DeltaArgs {
@@ -28,7 +32,9 @@ cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream);
 // Self-test GEMM used to validate descriptor conventions: C = A B with A a
 // 128 x K tile (K-major) and B either N x K (K-major, "score" form) or K x N
 // (MN-major, "accumulate" form); inputs through the same 4-D tensor maps.
-cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, float* c, int n, int k, bool bf16,
-                                 bool b_mn_major, int* err, cudaStream_t stream);
+// With a_tmem the A tile is copied into TMEM and the product is issued with A
+// from TMEM (the TS form).
+cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, const void* a, float* c, int n, int k,
+                                 bool bf16, bool b_mn_major, bool a_tmem, int* err, cudaStream_t stream);
 
 }  // namespace ttt

@@ -51,12 +51,13 @@ cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream) {
 // C[128 x N] = A[128 x K] * B, B K-major ([N x K] rows) or MN-major ([K x N] rows).
 struct SelftestParams {
   CUtensorMap ta, tb;
+  const uint16_t* a;  // row-major A, read directly when A sits in TMEM
   float* c;
   int n, k;
   int* err;
 };
 
-template <bool BF16, bool B_MN>
+template <bool BF16, bool B_MN, bool A_TMEM>
 __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_constant__ SelftestParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_cons
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -82,10 +83,27 @@ __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   Guard g{abort_flag, p.err};
+  if constexpr (A_TMEM) {
+    // Row r of A (this thread's lane) into TMEM columns 256 .. 256+K/2, two
+    // 16-bit elements per 32-bit column, low half first.
+    const int r = threadIdx.x;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t* arow = reinterpret_cast<const uint32_t*>(p.a) + r * (K / 2);
+    for (int c0 = 0; c0 < K / 2; c0 += 16) {
+      uint32_t w[16];
+      for (int j = 0; j < 16; ++j) w[j] = arow[c0 + j];
+      tmem_st16_raw(tmem + lane_off + 256 + c0, w);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
   if (threadIdx.x == 0) {
-    const int bytes = 128 * K * 2 + N * K * 2;
+    const int bytes = (A_TMEM ? 0 : 128 * K * 2) + N * K * 2;
     mbar_arrive_tx(bars + 0, bytes);
-    for (int pp = 0; pp < K / 64; ++pp) tma_load_4d(sA + pp * 128 * 128, &p.ta, bars + 0, pp * 64, 0, 0, 0);
+    if (!A_TMEM)
+      for (int pp = 0; pp < K / 64; ++pp) tma_load_4d(sA + pp * 128 * 128, &p.ta, bars + 0, pp * 64, 0, 0, 0);
     if (B_MN) {
       for (int pp = 0; pp < N / 64; ++pp) tma_load_4d(sB + pp * K * 128, &p.tb, bars + 0, pp * 64, 0, 0, 0);
     } else {
@@ -95,9 +113,12 @@ __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_cons
       tc_fence_after();
       const uint32_t idesc = idesc_f16(128, N, BF16, false, B_MN);
       for (int kk = 0; kk < K / 16; ++kk) {
-        const uint64_t da = desc_kmajor(smem_u32(sA), 128, kk);
         const uint64_t db = B_MN ? desc_mnmajor(smem_u32(sB), K, kk) : desc_kmajor(smem_u32(sB), N, kk);
-        umma_ss(tmem, da, db, idesc, kk > 0 ? 1u : 0u);
+        if constexpr (A_TMEM) {
+          umma_ts(tmem, tmem + 256 + kk * 8, db, idesc, kk > 0 ? 1u : 0u);
+        } else {
+          umma_ss(tmem, desc_kmajor(smem_u32(sA), 128, kk), db, idesc, kk > 0 ? 1u : 0u);
+        }
       }
       umma_commit(bars + 1);
     } else {
@@ -119,14 +140,15 @@ __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, float* c, int n, int k, bool bf16,
-                                 bool b_mn_major, int* err, cudaStream_t stream) {
+cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, const void* a, float* c, int n, int k,
+                                 bool bf16, bool b_mn_major, bool a_tmem, int* err, cudaStream_t stream) {
   SelftestParams p;
   p.ta = ta;
   p.tb = tb;
+  p.a = static_cast<const uint16_t*>(a);
   p.c = c;
   p.n = n;
   p.k = k;
@@ -138,10 +160,16 @@ cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, f
     kern<<<1, 128, smem, stream>>>(p);
     return cudaGetLastError();
   };
-  if (!bf16 && !b_mn_major) return launch(selftest_umma_kernel<false, false>);
-  if (!bf16 && b_mn_major) return launch(selftest_umma_kernel<false, true>);
-  if (bf16 && !b_mn_major) return launch(selftest_umma_kernel<true, false>);
-  return launch(selftest_umma_kernel<true, true>);
+  if (a_tmem) {
+    if (!bf16 && !b_mn_major) return launch(selftest_umma_kernel<false, false, true>);
+    if (!bf16 && b_mn_major) return launch(selftest_umma_kernel<false, true, true>);
+    if (bf16 && !b_mn_major) return launch(selftest_umma_kernel<true, false, true>);
+    return launch(selftest_umma_kernel<true, true, true>);
+  }
+  if (!bf16 && !b_mn_major) return launch(selftest_umma_kernel<false, false, false>);
+  if (!bf16 && b_mn_major) return launch(selftest_umma_kernel<false, true, false>);
+  if (bf16 && !b_mn_major) return launch(selftest_umma_kernel<true, false, false>);
+  return launch(selftest_umma_kernel<true, true, false>);
 }
 
 }  // namespace ttt

@@ -143,6 +143,17 @@ TTT_DEV void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A is M x K 16-bit, row m in TMEM lane m,
+// elements (m, 2j) and (m, 2j+1) packed low/high in 32-bit column j.
+TTT_DEV void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on `bar` when every tcgen05 op previously issued by this
 // thread has completed.
 TTT_DEV void umma_commit(uint64_t* bar) {
@@ -201,6 +212,18 @@ TTT_DEV void tmem_st16(uint32_t taddr, const float (&v)[16]) {
       "r"(__float_as_uint(v[15]))
       : "memory");
 }
+
+// Store 16 consecutive 32-bit TMEM columns of this thread's lane from raw
+// words (no wait; pair with tmem_wait_st()).
+TTT_DEV void tmem_st16_raw(uint32_t taddr, const uint32_t (&w)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n" ::"r"(taddr),
+      "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]),
+      "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
+      : "memory");
+}
+TTT_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor, 128-byte swizzle (the layout TMA writes for
