@@ -1,8 +1,7 @@
 // Key-major backward passes (sm_100a). One CTA owns 128 key rows of one head
-// and streams BM-query tiles (BM = 64, or 32 for the 128-wide double backward,
-// whose four resident key-side tiles leave room for two 32-row stages only).
-// Every score tile is computed transposed (keys x queries); the per-query
-// statistics (lse2, delta, gamma, rho) arrive with each streamed tile via TMA.
+// and streams 64-query tiles. Every score tile is computed transposed
+// (keys x queries), so the elementwise results are already oriented as the
+// A operand (M = keys) of the accumulate products.
 //
 //   kBwdKV  : dV = P^T dO,  dK = scale * dS^T Q
 //             (replaces _attn_bwd_dv_from_p_kernel and _attn_bwd_dk_kernel,
@@ -13,11 +12,25 @@
 //             reference approximates with torch.matmul in
 //             backward_stubs.py:435-514)
 //
-// Roles and pipeline as in attn_bwd_qm.cu: warps 0..7 elementwise (warp w:
-// TMEM lanes 32*(w%4)..+31, tile columns (w/4)*BM/2..+BM/2), warp 8 MMA issuer,
-// warp 9 TMA producer. In the double backward the streamed Q and u_q tiles are
-// stacked in one panel so that K [Q; u_q]^T produces [S^T | K u_q^T] as a
-// single N = 2*BM product.
+// Roles (320 threads): warps 0..7 elementwise (warp w: TMEM lanes
+// 32*(w%4)..+31, tile columns (w/4)*32..+32), warp 8 MMA issuer, warp 9 TMA
+// producer. The per-query statistics (lse2, delta, gamma, rho) of each tile
+// arrive with it through TMA and are read with broadcast 16-byte loads.
+//
+// Where the elementwise results live (ETM = "E in TMEM"):
+//   shared memory (kBwdKV, d=128): swizzled K-major tiles, SS products;
+//   a dedicated TMEM region (kBwdKV d=64, kBwd2KV d=64): packed 16-bit pairs,
+//     A-from-TMEM products, no ordering constraint;
+//   TMEM columns shared with the first score tiles (kBwd2KV d=128, where four
+//     64-wide score tiles and two 128-wide accumulators fill all 512 columns):
+//     each tile first issues the score products that do not touch those
+//     columns (dP^T, (dO u_v^T)^T), then the previous tile's accumulate
+//     products, waits for them to finish reading, and only then issues the
+//     products that overwrite the shared columns (K [Q; u_q]^T, u_k Q^T).
+//
+// In the double backward the streamed Q and u_q tiles are stacked in one
+// panel so that K [Q; u_q]^T produces [S^T | K u_q^T] as a single N=128
+// product (an M=128 UMMA with N <= 64 costs about as much as one with N=128).
 // Causal: query tiles that end before the CTA's first key are skipped.
 #include "attn_pipe.cuh"
 #include "kernels.h"
@@ -27,44 +40,64 @@ namespace ttt {
 template <int D, int KIND>
 struct KmCfg {
   static constexpr int BK = 128;  // keys per CTA (TMEM lanes)
+  static constexpr int BM = 64;   // queries per streamed tile
   static constexpr bool BWD2 = (KIND == kBwd2KV);
-  static constexpr int BM = (D == 128 && BWD2) ? 32 : 64;  // queries per streamed tile
-  static constexpr int NR = BWD2 ? 4 : 2;     // resident: K, V, (u_k, u_v)
-  static constexpr int NSTAT = BWD2 ? 4 : 2;  // streamed stats: lse2, delta, (gamma, rho)
-  static constexpr int NSC = BWD2 ? 4 : 2;    // score tiles: S^T, (G_dS^T,) dP^T, ((dO u_v^T)^T)
-  static constexpr int NE = BWD2 ? 3 : 2;     // P^T, dS^T | dS^T, G_S^T, G_dP^T
+  static constexpr int NR = BWD2 ? 4 : 2;   // resident: K, V, (u_k, u_v)
+  static constexpr int NSC = BWD2 ? 4 : 2;  // score tiles: S^T, (G_dS^T,) dP^T, ((dO u_v^T)^T)
+  static constexpr int NE = BWD2 ? 3 : 2;   // P^T, dS^T | dS^T, G_S^T, G_dP^T
   static constexpr int NA = 2;
   static constexpr int NCW = 8;
   static constexpr int NCT = NCW * 32;
   static constexpr int NTHREADS = NCT + 64;
   static constexpr int CPW = BM / 2;
   static constexpr int TILE_R = BK * D * 2;
-  // streamed: ST0 = [Q; u_q] (or Q), ST1 = dO, then the statistics rows
+  // streamed: ST0 = [Q; u_q] (or Q), ST1 = dO
   static constexpr int ST0_ROWS = BWD2 ? 2 * BM : BM;
   static constexpr int ST0_BYTES = ST0_ROWS * D * 2;
   static constexpr int ST1_BYTES = BM * D * 2;
+  static constexpr int NSTAT = BWD2 ? 4 : 2;  // lse2, delta, (gamma, rho) rows per stage
   static constexpr int STAT_BYTES = BM * 4;
   static constexpr int STAGE_TX = ST0_BYTES + ST1_BYTES + NSTAT * STAT_BYTES;  // bytes TMA delivers per stage
-  static constexpr int STAGE = (STAGE_TX + 1023) / 1024 * 1024;               // stage pitch keeps tiles 1024-aligned
-  static constexpr int TILE_E = BK * 64 * 2;                                    // one 64-column panel
-  static constexpr int NBUF = (2 * NSC * BM + NA * D <= 512) ? 2 : 1;
-  static constexpr int TMEM_USED = NBUF * NSC * BM + NA * D;
+  static constexpr int STAGE = (STAGE_TX + 1023) / 1024 * 1024;               // pitch keeps tiles 1024-aligned
+  static constexpr int TILE_E = BK * BM * 2;
+  static constexpr int E_COLS = BM / 2;  // TMEM columns of one packed 16-bit E tile
+  // TMEM layout
+  static constexpr bool ETM = BWD2 || D == 64;
+  static constexpr int NBUF_WANT = (2 * NSC * BM + NA * D + (ETM ? NE * E_COLS : 0) <= 512) ? 2 : 1;
+  static constexpr int NBUF = NBUF_WANT;
+  static constexpr int SC_COLS = NBUF * NSC * BM;
+  static constexpr int ACC_COL = SC_COLS;
+  static constexpr bool E_DEDICATED = ETM && (SC_COLS + NA * D + NE * E_COLS <= 512);
+  static constexpr bool E_OVERLAP = ETM && !E_DEDICATED;  // E shares score columns 0 .. NE*E_COLS
+  static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : 0;
+  static constexpr int TMEM_USED = SC_COLS + NA * D + (E_DEDICATED ? NE * E_COLS : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
-  static constexpr int FIXED = NR * TILE_R + NE * TILE_E + 16 * 8 + 16 + 1024 + STAGE_TX;
-  static constexpr int NSTAGE = (FIXED + 3 * STAGE <= 232448) ? 4 : (FIXED + 2 * STAGE <= 232448) ? 3 : 2;
+  static_assert(!E_OVERLAP || NBUF == 1, "overlapping E needs a single score buffer");
+  static constexpr int E_SMEM = ETM ? 0 : NE * TILE_E;
+  static constexpr int BAR_BYTES = 20 * 8;
+  static constexpr int FIXED = NR * TILE_R + E_SMEM + BAR_BYTES + (STAGE_TX - STAGE);
+  static constexpr int NSTAGE = (FIXED + 4 * STAGE + 1024 <= 232448) ? 4 : (FIXED + 3 * STAGE + 1024 <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
   static constexpr int OFF_E = OFF_R + NR * TILE_R;
-  static constexpr int OFF_S = OFF_E + NE * TILE_E;  // stages last; the last one needs no padding
-  static constexpr int OFF_BAR = OFF_S + (NSTAGE - 1) * STAGE + STAGE_TX;
-  static constexpr int NBAR = 16;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int OFF_S = OFF_E + E_SMEM;
+  static constexpr int OFF_BAR = OFF_S + (NSTAGE - 1) * STAGE + STAGE_TX;  // the last stage needs no padding
+  static constexpr int BODY = OFF_BAR + BAR_BYTES;
+  // Reserve room to realign the dynamic shared-memory base to 1024 bytes when
+  // it fits; otherwise the kernel requires (and checks) an aligned base.
+  static constexpr int PAD = (BODY + 1024 <= 232448) ? 1024 : 0;
+  static constexpr int SMEM = BODY + PAD;
   static_assert(SMEM <= 232448, "key-major tile set exceeds shared memory");
   static_assert(ST0_BYTES % 1024 == 0 && ST1_BYTES % 1024 == 0, "streamed tiles must stay 1024-aligned");
+  // score tile columns within a buffer
   static constexpr int C_S = 0, C_GDS = BWD2 ? BM : 0, C_DP = BWD2 ? 2 * BM : BM, C_UV = 3 * BM;
 };
 
-int km_tile_rows(int d, int kind) { return (d == 128 && kind == kBwd2KV) ? 32 : 64; }
+int km_tile_rows(int d, int kind) {
+  (void)d;
+  (void)kind;
+  return 64;
+}
 
 template <int D, bool BF16, bool CAUSAL, int KIND>
 __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(const __grid_constant__ KParams p) {
@@ -72,28 +105,35 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   constexpr int BM = C::BM, BK = C::BK, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE, CPW = C::CPW;
   constexpr int SR0 = C::ST0_ROWS;
   constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = C::PAD ? align1024(smem_raw) : smem_raw;
+  if (C::PAD == 0 && (smem_u32(smem_raw) & 1023u) != 0) {
+    // no room to realign: refuse to run on a misaligned base (the swizzled
+    // tiles would be read wrongly) and report it through the error word
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrMisaligned);
+    return;
+  }
   uint8_t* sR = smem + C::OFF_R;
   uint8_t* sS = smem + C::OFF_S;
   uint8_t* sE = smem + C::OFF_E;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
-  uint64_t* l_full = bars + 1;   // [4]
-  uint64_t* l_empty = bars + 5;  // [4]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_free = bars + 11;  // [2] (NCT arrivals)
-  uint64_t* e_full = bars + 13;  // NCT arrivals
-  uint64_t* e_empty = bars + 14;
+  uint64_t* l_full = bars + 1;    // [4]
+  uint64_t* l_empty = bars + 5;   // [4]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_free = bars + 11;   // [2] (NCT arrivals)
+  uint64_t* e_full = bars + 13;   // NCT arrivals
+  uint64_t* e_empty = bars + 14;  // accumulate products of a tile finished (E consumed)
   uint64_t* acc_full = bars + 15;
   uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* e_done = bars + 17;   // MMA thread's own wait point for E_OVERLAP
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto tileR = [&](int t) { return sR + t * C::TILE_R; };
   auto st0 = [&](int s) { return sS + s * C::STAGE; };
   auto st1 = [&](int s) { return sS + s * C::STAGE + C::ST0_BYTES; };
   auto statS = [&](int s, int t) {
-    return reinterpret_cast<float*>(sS + s * C::STAGE + C::ST0_BYTES + C::ST1_BYTES + t * C::STAT_BYTES);
+    return reinterpret_cast<const float*>(sS + s * C::STAGE + C::ST0_BYTES + C::ST1_BYTES + t * C::STAT_BYTES);
   };
   auto tileE = [&](int t) { return sE + t * C::TILE_E; };
 
@@ -108,7 +148,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const int n_tiles = n_q - qt0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 17; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     mbar_init(e_full, C::NCT);
@@ -126,8 +166,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tAcc0 = tmem + NBUF * C::NSC * BM;  // dK / dd_K
-  const uint32_t tAcc1 = tAcc0 + D;                  // dV / dd_V
+  const uint32_t tAcc0 = tmem + C::ACC_COL;  // dK / dd_K
+  const uint32_t tAcc1 = tAcc0 + D;          // dV / dd_V
+  const uint32_t tE = tmem + C::E_COL;       // packed E tiles (ETM)
   Guard g{abort_flag, p.err};
 
   if (warp == WARP_LOAD) {
@@ -153,7 +194,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           if constexpr (C::BWD2)
             tma_load_4d(st0(s) + pp * SR0 * 128 + BM * 128, &p.str[2], l_full + s, pp * 64, qrow, hidx, bidx);
         }
-        for (int t = 0; t < C::NSTAT; ++t) tma_load_2d(statS(s, t), &p.st[t], l_full + s, qrow, bh);
+        for (int t = 0; t < C::NSTAT; ++t)
+          tma_load_2d(const_cast<float*>(statS(s, t)), &p.st[t], l_full + s, qrow, bh);
         issued[s] = n + 1;
       }
       mbar_drain(res_full, 0);
@@ -168,75 +210,100 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       constexpr uint32_t id_acc = idesc_f16(128, D, BF16, false, true);
       const uint32_t aK = smem_u32(tileR(0)), aV = smem_u32(tileR(1));
       const uint32_t aUK = C::BWD2 ? smem_u32(tileR(2)) : 0u, aUV = C::BWD2 ? smem_u32(tileR(3)) : 0u;
-      auto issue_scores = [&](int n) -> bool {
-        const int sb = n % NBUF, s = n % NSTAGE;
-        if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2)) return false;
-        if (n >= NBUF && !mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3)) return false;
-        tc_fence_after();
-        const uint32_t base = tmem + sb * C::NSC * BM;
-        const uint32_t b0 = smem_u32(st0(s)), b1 = smem_u32(st1(s));
+      // Score products whose output columns never hold E: dP^T (and (dO u_v^T)^T).
+      auto scores_free_cols = [&](uint32_t base, int s) {
+        const uint32_t b1 = smem_u32(st1(s));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(base + C::C_DP, desc_kmajor(aV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
         if constexpr (C::BWD2) {
-          // [S^T | K u_q^T] = K [Q; u_q]^T ; G_dS^T/scale += u_k Q^T ; dP^T = V dO^T ; (dO u_v^T)^T = u_v dO^T
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss(base + C::C_UV, desc_kmajor(aUV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
+        }
+      };
+      // Score products into columns that E may share: S^T (and G_dS^T).
+      auto scores_e_cols = [&](uint32_t base, int s) {
+        const uint32_t b0 = smem_u32(st0(s));
+        if constexpr (C::BWD2) {
+          // [S^T | K u_q^T] = K [Q; u_q]^T ; G_dS^T/scale += u_k Q^T
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_S, desc_kmajor(aK, BK, kk), desc_kmajor(b0, SR0, kk), id_n2, kk > 0);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_GDS, desc_kmajor(aUK, BK, kk), desc_kmajor(b0, SR0, kk), id_n1, 1u);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_DP, desc_kmajor(aV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_UV, desc_kmajor(aUV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_S, desc_kmajor(aK, BK, kk), desc_kmajor(b0, SR0, kk), id_n1, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_DP, desc_kmajor(aV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
         }
-        umma_commit(s_full + sb);
-        return true;
       };
-      auto issue_acc = [&](int n) -> bool {
+      auto acc_products = [&](int n) {
         const int s = n % NSTAGE;
-        if (!mbar_wait(e_full, n & 1, g, 4)) return false;
-        tc_fence_after();
         const uint32_t bQ = smem_u32(st0(s)), bDO = smem_u32(st1(s));
-        const uint32_t e0 = smem_u32(tileE(0)), e1 = smem_u32(tileE(1));
+        const uint32_t acc_first = n > 0 ? 1u : 0u;
         if constexpr (!C::BWD2) {
           // dV += P^T dO ; dK += dS^T Q
 #pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ss(tAcc1, desc_kmajor(e0, BK, kk), desc_mnmajor(bDO, BM, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e1, BK, kk), desc_mnmajor(bQ, SR0, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BM / 16; ++kk) {
+            const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
+            if constexpr (C::ETM) {
+              umma_ts(tAcc1, tE + 0 * C::E_COLS + kk * 8, desc_mnmajor(bDO, BM, kk), id_acc, a);
+              umma_ts(tAcc0, tE + 1 * C::E_COLS + kk * 8, desc_mnmajor(bQ, SR0, kk), id_acc, a);
+            } else {
+              umma_ss(tAcc1, desc_kmajor(smem_u32(tileE(0)), BK, kk), desc_mnmajor(bDO, BM, kk), id_acc, a);
+              umma_ss(tAcc0, desc_kmajor(smem_u32(tileE(1)), BK, kk), desc_mnmajor(bQ, SR0, kk), id_acc, a);
+            }
+          }
         } else {
-          // dd_K += dS^T u_q + G_S^T Q ; dd_V += G_dP^T dO
-          const uint32_t bUQ = bQ + BM * 128, e2 = smem_u32(tileE(2));
+          // dd_K += dS^T u_q + G_S^T Q ; dd_V += G_dP^T dO   (E in TMEM)
+          const uint32_t bUQ = bQ + BM * 128;
 #pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e0, BK, kk), desc_mnmajor(bUQ, SR0, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e1, BK, kk), desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
-#pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ss(tAcc1, desc_kmajor(e2, BK, kk), desc_mnmajor(bDO, BM, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BM / 16; ++kk) {
+            const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
+            umma_ts(tAcc0, tE + 0 * C::E_COLS + kk * 8, desc_mnmajor(bUQ, SR0, kk), id_acc, a);
+            umma_ts(tAcc0, tE + 1 * C::E_COLS + kk * 8, desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
+            umma_ts(tAcc1, tE + 2 * C::E_COLS + kk * 8, desc_mnmajor(bDO, BM, kk), id_acc, a);
+          }
         }
-        umma_commit(e_empty);
-        umma_commit(l_empty + s);
-        return true;
       };
       bool ok = mbar_wait(res_full, 0, g, 1);
-      for (int n = 0; ok && n < n_tiles; ++n) {
-        ok = issue_scores(n);
-        if (ok && n >= 1) ok = issue_acc(n - 1);
+      for (int n = 0; ok && n <= n_tiles; ++n) {
+        const bool has_scores = n < n_tiles;
+        const int sb = n % NBUF, s = n % NSTAGE;
+        const uint32_t base = tmem + sb * C::NSC * BM;
+        if (has_scores) {
+          if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+          if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+          tc_fence_after();
+          if constexpr (C::E_OVERLAP) {
+            scores_free_cols(base, s);
+          } else {
+            scores_e_cols(base, s);
+            scores_free_cols(base, s);
+            umma_commit(s_full + sb);
+          }
+        }
+        if (n >= 1) {
+          // accumulate products of tile n-1
+          if (!(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
+          tc_fence_after();
+          acc_products(n - 1);
+          umma_commit(e_empty);
+          umma_commit(l_empty + (n - 1) % NSTAGE);
+          if constexpr (C::E_OVERLAP) umma_commit(e_done);
+        }
+        if constexpr (C::E_OVERLAP) {
+          if (has_scores) {
+            // E(n-1) must be fully read before S^T / G_dS^T of tile n overwrite its columns.
+            if (n >= 1 && !(ok = mbar_wait(e_done, (n - 1) & 1, g, 5))) break;
+            tc_fence_after();
+            scores_e_cols(base, s);
+            umma_commit(s_full + sb);
+          }
+        }
       }
-      if (ok) ok = issue_acc(n_tiles - 1);
       if (ok) umma_commit(acc_full);
       umma_commit(drain);
       mbar_drain(drain, 0);
@@ -253,9 +320,11 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
       const int sb = n % NBUF, s = n % NSTAGE;
+      const int qt = qt0 + n;
+      const int qcol0 = qt * BM + c0;
       if (!mbar_wait(s_full + sb, (n / NBUF) & 1, g, 6)) { ok = false; break; }
-      // The per-query statistics were delivered by TMA on l_full[s]; that
-      // phase cannot advance until this tile's elementwise step is done.
+      // The per-query statistics arrived by TMA on l_full[s]; that phase cannot
+      // advance until this tile's elementwise step is done.
       if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 9)) { ok = false; break; }
       tc_fence_after();
       const uint32_t base = tmem + lane_off + sb * C::NSC * BM + c0;
@@ -276,8 +345,6 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       tc_fence_before();
       mbar_arrive(s_free + sb);
 
-      const int qt = qt0 + n;
-      const int qcol0 = qt * BM + c0;
       const bool need_mask = key_edge || (CAUSAL && qt * BM < k0 + BK - 1);
       const float4* st_lse = reinterpret_cast<const float4*>(statS(s, 0) + c0);
       const float4* st_del = reinterpret_cast<const float4*>(statS(s, 1) + c0);
@@ -285,8 +352,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       const float4* st_rho = reinterpret_cast<const float4*>(statS(s, C::BWD2 ? 3 : 0) + c0);
 #pragma unroll
       for (int q4 = 0; q4 < CPW / 4; ++q4) {
-        const float4 l4 = st_lse[q4];
-        const float4 d4 = st_del[q4];
+        const float4 l4 = st_lse[q4], d4 = st_del[q4];
         float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), r4 = g4;
         if constexpr (C::BWD2) {
           g4 = st_gam[q4];
@@ -294,8 +360,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         }
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
         const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
-        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+        const float gv4[4] = {g4.x, g4.y, g4.z, g4.w};
+        const float rv4[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int e = q4 * 4 + u;
@@ -308,20 +374,39 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             dp[e] = pr * (dp[e] - dv[u]);  // dS^T
             sv[e] = pr;                    // P^T
           } else {
+            const float gv = gv4[u], rv = rv4[u];
             const float dpm = dp[e] - dv[u];
             const float gds = gd[e] * scale;
-            const float gP = fmaf(gds, dpm, fmaf(-gv[u], dp[e], uv[e]));
-            sv[e] = pr * dpm;             // dS^T
-            dp[e] = pr * (gP - rv[u]);    // G_S^T
-            gd[e] = pr * (gds - gv[u]);   // G_dP^T
+            const float gP = fmaf(gds, dpm, fmaf(-gv, dp[e], uv[e]));
+            sv[e] = pr * dpm;           // dS^T
+            dp[e] = pr * (gP - rv);     // G_S^T
+            gd[e] = pr * (gds - gv);    // G_dP^T
           }
         }
       }
       if (n >= 1 && !mbar_wait(e_empty, (n - 1) & 1, g, 7)) { ok = false; break; }
-      store_cols<BF16, CPW>(tileE(0), BK, r, c0, sv);
-      store_cols<BF16, CPW>(tileE(1), BK, r, c0, dp);
-      if constexpr (C::BWD2) store_cols<BF16, CPW>(tileE(2), BK, r, c0, gd);
-      fence_async_smem();
+      if constexpr (C::ETM) {
+        // packed 16-bit pairs: this thread's 32 columns -> 16 TMEM columns per E tile
+        const uint32_t eb = tE + lane_off + (c0 >> 1);
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(sv[2 * j], sv[2 * j + 1]);
+        tmem_st16_raw(eb + 0 * C::E_COLS, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(dp[2 * j], dp[2 * j + 1]);
+        tmem_st16_raw(eb + 1 * C::E_COLS, w);
+        if constexpr (C::BWD2) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(gd[2 * j], gd[2 * j + 1]);
+          tmem_st16_raw(eb + 2 * C::E_COLS, w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+      } else {
+        store_cols<BF16, CPW>(tileE(0), BK, r, c0, sv);
+        store_cols<BF16, CPW>(tileE(1), BK, r, c0, dp);
+        fence_async_smem();
+      }
       mbar_arrive(e_full);
     }
     if (ok && mbar_wait(acc_full, 0, g, 8)) {

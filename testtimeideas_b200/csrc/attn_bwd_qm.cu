@@ -57,17 +57,22 @@ struct QmCfg {
   static constexpr int STAGE = 2 * ST_BYTES;
   static constexpr int TILE_R = BM * D * 2;
   static constexpr int TILE_E = BM * 64 * 2;  // one 64-column panel (BN <= 64 columns used)
+  // Q and u_q (A operands only) in TMEM for the 128-wide double backward, which
+  // frees shared memory for a third stage
+  static constexpr bool RES_TMEM = (KIND == kBwd2Q) && D == 128 && !GDO;
+  static constexpr int NR_SMEM = RES_TMEM ? 1 : NR;  // only dO stays in shared memory
   // elementwise results in the ST1 part of their own stage when they fit
   static constexpr bool EIS = (KIND == kBwd2Q) && (NE * TILE_E <= ST_BYTES);
   static constexpr int E_BYTES = EIS ? 0 : NE * TILE_E;
   static constexpr int NBUF = (2 * NSC * BN + NA * D <= 512) ? 2 : 1;
-  static constexpr int TMEM_USED = NBUF * NSC * BN + NA * D;
+  static constexpr int RES_COL = NBUF * NSC * BN + NA * D;  // packed Q, u_q (RES_TMEM)
+  static constexpr int TMEM_USED = RES_COL + (RES_TMEM ? D : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
-  static constexpr int FIXED = NR * TILE_R + E_BYTES + 16 * 8 + 16 + 1024;
+  static constexpr int FIXED = NR_SMEM * TILE_R + E_BYTES + 16 * 8 + 16 + 1024;
   static constexpr int NSTAGE = (FIXED + 4 * STAGE <= 232448) ? 4 : (FIXED + 3 * STAGE <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
-  static constexpr int OFF_S = OFF_R + NR * TILE_R;
+  static constexpr int OFF_S = OFF_R + NR_SMEM * TILE_R;
   static constexpr int OFF_E = OFF_S + NSTAGE * STAGE;
   static constexpr int OFF_BAR = OFF_E + E_BYTES;
   static constexpr int NBAR = 16;
@@ -106,7 +111,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   static_assert(17 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
-  auto tileR = [&](int t) { return sR + t * C::TILE_R; };
+  auto tileR = [&](int t) { return sR + (C::RES_TMEM ? 0 : t) * C::TILE_R; };
   auto tileS = [&](int s, int t) { return sS + s * C::STAGE + t * C::ST_BYTES; };
   auto tileE = [&](int s, int t) { return C::EIS ? tileS(s, 1) + t * C::TILE_E : sE + t * C::TILE_E; };
 
@@ -124,6 +129,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     mbar_init(e_full, C::NCT);
+    if (C::RES_TMEM) mbar_init(res_full, 1 + C::NCT);  // dO by TMA + Q, u_q copied to TMEM by the compute warps
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
     fence_mbar_init();
@@ -140,6 +146,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const uint32_t tmem = *tmem_slot;
   const uint32_t tAcc0 = tmem + NBUF * C::NSC * BN;
   const uint32_t tAcc1 = tAcc0 + D;
+  const uint32_t tQ = tmem + C::RES_COL, tUQ = tQ + D / 2;  // packed resident A operands (RES_TMEM)
   Guard g{abort_flag, p.err};
 
   if (warp == WARP_LOAD) {
@@ -149,10 +156,12 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       for (int t = 0; t < C::NR; ++t) tma_prefetch(&p.own[t]);
       for (int t = 0; t < NSTR; ++t) tma_prefetch(&p.str[t]);
       int issued[4] = {0, 0, 0, 0};
-      mbar_arrive_tx(res_full, C::NR * C::TILE_R);
-      for (int t = 0; t < C::NR; ++t)
+      mbar_arrive_tx(res_full, C::NR_SMEM * C::TILE_R);
+      for (int t = 0; t < C::NR; ++t) {
+        if (C::RES_TMEM && t != 1) continue;  // Q and u_q go to TMEM through the compute warps
         for (int pp = 0; pp < NP; ++pp)
           tma_load_4d(tileR(t) + pp * BM * 128, &p.own[t], res_full, pp * 64, q0, hidx, bidx);
+      }
       for (int n = 0; n < n_tiles; ++n) {
         const int s = n % NSTAGE;
         if (n >= NSTAGE && !mbar_wait(l_empty + s, ((n / NSTAGE) - 1) & 1, g, 1)) break;
@@ -186,12 +195,21 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         const uint32_t b0 = smem_u32(tileS(s, 0)), b1 = smem_u32(tileS(s, 1));
         if constexpr (C::BWD2) {
           // [S | Q u_k^T] = Q [K; u_k]^T ; G_dS/scale += u_q K^T ; [dP | dO u_v^T] = dO [V; u_v]^T
+          if constexpr (C::RES_TMEM) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_S, desc_kmajor(aQ, BM, kk), desc_kmajor(b0, SR, kk), id_n2, kk > 0);
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_ts(base + C::C_S, tQ + kk * 8, desc_kmajor(b0, SR, kk), id_n2, kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_GDS, desc_kmajor(aUQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, 1u);
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_ts(base + C::C_GDS, tUQ + kk * 8, desc_kmajor(b0, SR, kk), id_n1, 1u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_ss(base + C::C_S, desc_kmajor(aQ, BM, kk), desc_kmajor(b0, SR, kk), id_n2, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_ss(base + C::C_GDS, desc_kmajor(aUQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, 1u);
+          }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n2, kk > 0);
@@ -272,6 +290,37 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       rho = p.rho[sidx];
     }
     float a_g = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+    if constexpr (C::RES_TMEM) {
+      // This thread's row, columns half*D/2 .. +D/2, of Q (slot 0) and u_q (slot 2):
+      // 16-bit pairs in memory are already the packed TMEM operand format.
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int slot = t == 0 ? 0 : 2;
+        uint32_t w[D / 4];
+        if (row < T) {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              p.raw[slot] + static_cast<int64_t>(bidx) * p.raw_sb[slot] + static_cast<int64_t>(hidx) * p.raw_sh[slot] +
+              static_cast<int64_t>(row) * p.raw_st[slot] + half * (D / 2));
+#pragma unroll
+          for (int v = 0; v < D / 16; ++v) {
+            const uint4 x = src[v];
+            w[4 * v + 0] = x.x;
+            w[4 * v + 1] = x.y;
+            w[4 * v + 2] = x.z;
+            w[4 * v + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int v = 0; v < D / 4; ++v) w[v] = 0u;
+        }
+        const uint32_t dst = (t == 0 ? tQ : tUQ) + lane_off + half * (D / 4);
+#pragma unroll
+        for (int c16 = 0; c16 < D / 4; c16 += 16) tmem_st16_raw(dst + c16, *reinterpret_cast<uint32_t(*)[16]>(w + c16));
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(res_full);
+    }
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
       const int sb = n % NBUF, s = n % NSTAGE;

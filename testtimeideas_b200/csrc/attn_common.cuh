@@ -32,6 +32,10 @@ struct KParams {
   CUtensorMap str[4];
   // fp32 [b*h, t_pad] row statistics streamed per column tile (key-major).
   CUtensorMap st[4];
+  // Raw views of the owner-side inputs (same slots as own[]), for kernels that
+  // stage them in tensor memory with plain loads.
+  const uint16_t* raw[4];
+  int64_t raw_sb[4], raw_sh[4], raw_st[4];
   // Raw row statistics (query-major kernels read their own rows directly).
   const float* lse2;
   const float* delta;

@@ -109,6 +109,13 @@ void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
   k.err = err;
 }
 
+void set_raw(KParams& k, int slot, const ttt_view& v) {
+  k.raw[slot] = static_cast<const uint16_t*>(v.ptr);
+  k.raw_sb[slot] = v.sb;
+  k.raw_sh[slot] = v.sh;
+  k.raw_st[slot] = v.st;
+}
+
 void set_out0(KParams& k, const ttt_view& v) {
   k.out0 = static_cast<uint16_t*>(v.ptr);
   k.o0_sb = v.sb;
@@ -320,6 +327,9 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   TTT_TRY(encode_view(&kq.own[0], a->q, pb, 128));
   TTT_TRY(encode_view(&kq.own[1], a->dout, pb, 128));
   TTT_TRY(encode_view(&kq.own[2], a->uq, pb, 128));
+  set_raw(kq, 0, a->q);
+  set_raw(kq, 1, a->dout);
+  set_raw(kq, 2, a->uq);
   auto encode_stream_q = [&](int cols) -> int {
     TTT_TRY(encode_view(&kq.str[0], a->k, pb, cols));
     TTT_TRY(encode_view(&kq.str[1], a->v, pb, cols));

@@ -23,6 +23,7 @@ namespace ttt {
 // Error word layout written by kernels into the caller's err_flag (int32):
 // 0 = ok; otherwise kErrTimeout | (site << 8) | (blockIdx-derived low bits).
 constexpr int kErrTimeout = 0x40000000;
+constexpr int kErrMisaligned = 0x20000000;  // dynamic shared memory base not 1024-aligned
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 TTT_DEV uint32_t smem_u32(const void* p) {
