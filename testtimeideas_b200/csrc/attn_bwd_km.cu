@@ -317,6 +317,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float c = p.scale_log2, scale = p.scale;
     const bool key_edge = k0 + BK > T;
+    const F2 C2 = f2s(c), SC2 = f2s(scale);
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
       const int sb = n % NBUF, s = n % NSTAGE;
@@ -358,29 +359,33 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           g4 = st_gam[q4];
           r4 = st_rho[q4];
         }
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-        const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-        const float gv4[4] = {g4.x, g4.y, g4.z, g4.w};
-        const float rv4[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = q4 * 4 + u;
-          float pr = fast_exp2(fmaf(sv[e], c, -lv[u]));
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int e = q4 * 4 + h2 * 2;
+          const F2 L = h2 ? f2(l4.z, l4.w) : f2(l4.x, l4.y);
+          const F2 DEL = h2 ? f2(d4.z, d4.w) : f2(d4.x, d4.y);
+          float x0, x1;
+          split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), L), x0, x1);
+          float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           if (need_mask) {
             const int qi = qcol0 + e;
-            pr = ((key < T) && (!CAUSAL || key <= qi)) ? pr : 0.f;
+            p0 = ((key < T) && (!CAUSAL || key <= qi)) ? p0 : 0.f;
+            p1 = ((key < T) && (!CAUSAL || key <= qi + 1)) ? p1 : 0.f;
           }
+          const F2 PR = f2(p0, p1), DP = f2(dp[e], dp[e + 1]);
           if constexpr (!C::BWD2) {
-            dp[e] = pr * (dp[e] - dv[u]);  // dS^T
-            sv[e] = pr;                    // P^T
+            split(mul2(PR, sub2(DP, DEL)), dp[e], dp[e + 1]);  // dS^T
+            sv[e] = p0;                                       // P^T
+            sv[e + 1] = p1;
           } else {
-            const float gv = gv4[u], rv = rv4[u];
-            const float dpm = dp[e] - dv[u];
-            const float gds = gd[e] * scale;
-            const float gP = fmaf(gds, dpm, fmaf(-gv, dp[e], uv[e]));
-            sv[e] = pr * dpm;           // dS^T
-            dp[e] = pr * (gP - rv);     // G_S^T
-            gd[e] = pr * (gds - gv);    // G_dP^T
+            const F2 GAM = h2 ? f2(g4.z, g4.w) : f2(g4.x, g4.y);
+            const F2 RHO = h2 ? f2(r4.z, r4.w) : f2(r4.x, r4.y);
+            const F2 DPM = sub2(DP, DEL);
+            const F2 GDS = mul2(f2(gd[e], gd[e + 1]), SC2);
+            const F2 GP = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), mul2(GAM, DP)));
+            split(mul2(PR, DPM), sv[e], sv[e + 1]);              // dS^T
+            split(mul2(PR, sub2(GP, RHO)), dp[e], dp[e + 1]);    // G_S^T
+            split(mul2(PR, sub2(GDS, GAM)), gd[e], gd[e + 1]);   // G_dP^T
           }
         }
       }

@@ -42,7 +42,7 @@ template <int D, int KIND, bool GDO>
 struct QmCfg {
   static constexpr int BM = 128;
   static constexpr bool BWD2 = (KIND != kBwdQ);
-  static constexpr int BN = (D == 128 && KIND == kBwd2Q && GDO) ? 32 : 64;
+  static constexpr int BN = KIND == kBwdQ ? 128 : ((D == 128 && KIND == kBwd2Q && GDO) ? 32 : 64);
   static constexpr int NR = BWD2 ? 3 : 2;    // resident: Q, dO, (u_q)
   static constexpr int NSC = BWD2 ? 4 : 2;   // score tiles: S, (G_dS,) dP, (dO u_v^T)
   static constexpr int NE = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 4 : 2));
@@ -56,17 +56,22 @@ struct QmCfg {
   static constexpr int ST_BYTES = ST_ROWS * D * 2;
   static constexpr int STAGE = 2 * ST_BYTES;
   static constexpr int TILE_R = BM * D * 2;
-  static constexpr int TILE_E = BM * 64 * 2;  // one 64-column panel (BN <= 64 columns used)
-  // Q and u_q (A operands only) in TMEM for the 128-wide double backward, which
-  // frees shared memory for a third stage
-  static constexpr bool RES_TMEM = (KIND == kBwd2Q) && D == 128 && !GDO;
-  static constexpr int NR_SMEM = RES_TMEM ? 1 : NR;  // only dO stays in shared memory
+  static constexpr int TILE_E = BM * (BN > 64 ? BN : 64) * 2;  // whole 64-column panels
+  // Owner-side operands that are only ever A operands of score products can sit
+  // in TMEM (A-from-TMEM products), which frees shared memory for deeper
+  // staging: Q and dO for the dq pass; Q and u_q for the 128-wide double backward.
+  static constexpr bool RT_Q = (KIND == kBwdQ) || (KIND == kBwd2Q && D == 128 && !GDO);
+  static constexpr bool RT_DO = (KIND == kBwdQ);
+  static constexpr bool RT_UQ = (KIND == kBwd2Q && D == 128 && !GDO);
+  static constexpr bool RES_TMEM = RT_Q || RT_DO || RT_UQ;
+  static constexpr int NR_TMEM = (RT_Q ? 1 : 0) + (RT_DO ? 1 : 0) + (RT_UQ ? 1 : 0);
+  static constexpr int NR_SMEM = NR - NR_TMEM;
   // elementwise results in the ST1 part of their own stage when they fit
-  static constexpr bool EIS = (KIND == kBwd2Q) && (NE * TILE_E <= ST_BYTES);
+  static constexpr bool EIS = (KIND == kBwd2Q || KIND == kBwdQ) && (NE * TILE_E <= ST_BYTES);
   static constexpr int E_BYTES = EIS ? 0 : NE * TILE_E;
   static constexpr int NBUF = (2 * NSC * BN + NA * D <= 512) ? 2 : 1;
   static constexpr int RES_COL = NBUF * NSC * BN + NA * D;  // packed Q, u_q (RES_TMEM)
-  static constexpr int TMEM_USED = RES_COL + (RES_TMEM ? D : 0);
+  static constexpr int TMEM_USED = RES_COL + NR_TMEM * (D / 2);
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
   static constexpr int FIXED = NR_SMEM * TILE_R + E_BYTES + 16 * 8 + 16 + 1024;
@@ -82,7 +87,7 @@ struct QmCfg {
   static constexpr int C_S = 0, C_GDS = BWD2 ? BN : 0, C_DP = BWD2 ? 2 * BN : BN, C_UV = 3 * BN;
 };
 
-int qm_tile_cols(int d, int kind, bool gdo) { return (d == 128 && kind == kBwd2Q && gdo) ? 32 : 64; }
+int qm_tile_cols(int d, int kind, bool gdo) { return kind == kBwdQ ? 128 : ((d == 128 && kind == kBwd2Q && gdo) ? 32 : 64); }
 
 template <int D, bool BF16, bool CAUSAL, int KIND, bool GDO>
 __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kernel(const __grid_constant__ KParams p) {
@@ -111,7 +116,13 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   static_assert(17 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
-  auto tileR = [&](int t) { return sR + (C::RES_TMEM ? 0 : t) * C::TILE_R; };
+  // resident tiles kept in shared memory, packed in slot order
+  auto in_tmem = [&](int t) { return (t == 0 && C::RT_Q) || (t == 1 && C::RT_DO) || (t == 2 && C::RT_UQ); };
+  auto tileR = [&](int t) {
+    int idx = 0;
+    for (int u = 0; u < t; ++u) idx += in_tmem(u) ? 0 : 1;
+    return sR + idx * C::TILE_R;
+  };
   auto tileS = [&](int s, int t) { return sS + s * C::STAGE + t * C::ST_BYTES; };
   auto tileE = [&](int s, int t) { return C::EIS ? tileS(s, 1) + t * C::TILE_E : sE + t * C::TILE_E; };
 
@@ -129,7 +140,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     mbar_init(e_full, C::NCT);
-    if (C::RES_TMEM) mbar_init(res_full, 1 + C::NCT);  // dO by TMA + Q, u_q copied to TMEM by the compute warps
+    if (C::RES_TMEM) mbar_init(res_full, 1 + C::NCT);  // TMA + the compute warps' copies into TMEM
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
     fence_mbar_init();
@@ -146,7 +157,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const uint32_t tmem = *tmem_slot;
   const uint32_t tAcc0 = tmem + NBUF * C::NSC * BN;
   const uint32_t tAcc1 = tAcc0 + D;
-  const uint32_t tQ = tmem + C::RES_COL, tUQ = tQ + D / 2;  // packed resident A operands (RES_TMEM)
+  // packed resident A operands in TMEM (RES_TMEM), in slot order Q, dO, u_q
+  const uint32_t tQ = tmem + C::RES_COL;
+  const uint32_t tDO = tQ + (C::RT_Q ? D / 2 : 0);
+  const uint32_t tUQ = tDO + (C::RT_DO ? D / 2 : 0);
   Guard g{abort_flag, p.err};
 
   if (warp == WARP_LOAD) {
@@ -158,7 +172,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       int issued[4] = {0, 0, 0, 0};
       mbar_arrive_tx(res_full, C::NR_SMEM * C::TILE_R);
       for (int t = 0; t < C::NR; ++t) {
-        if (C::RES_TMEM && t != 1) continue;  // Q and u_q go to TMEM through the compute warps
+        if (in_tmem(t)) continue;  // copied to TMEM by the compute warps
         for (int pp = 0; pp < NP; ++pp)
           tma_load_4d(tileR(t) + pp * BM * 128, &p.own[t], res_full, pp * 64, q0, hidx, bidx);
       }
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         const uint32_t b0 = smem_u32(tileS(s, 0)), b1 = smem_u32(tileS(s, 1));
         if constexpr (C::BWD2) {
           // [S | Q u_k^T] = Q [K; u_k]^T ; G_dS/scale += u_q K^T ; [dP | dO u_v^T] = dO [V; u_v]^T
-          if constexpr (C::RES_TMEM) {
+          if constexpr (C::RT_Q) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
               umma_ts(base + C::C_S, tQ + kk * 8, desc_kmajor(b0, SR, kk), id_n2, kk > 0);
@@ -213,6 +227,13 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n2, kk > 0);
+        } else if constexpr (C::RT_Q && C::RT_DO) {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ts(base + C::C_S, tQ + kk * 8, desc_kmajor(b0, SR, kk), id_n1, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ts(base + C::C_DP, tDO + kk * 8, desc_kmajor(b1, SR, kk), id_n1, kk > 0);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
@@ -289,13 +310,14 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       gam = p.gamma[sidx];
       rho = p.rho[sidx];
     }
-    float a_g = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+    const F2 C2 = f2s(c), SC2 = f2s(scale), LSE2 = f2s(lse), DEL2 = f2s(del), GAM2 = f2s(gam), RHO2 = f2s(rho);
+    F2 AG = f2s(0.f), A2 = AG, A3 = AG, A4 = AG;  // stats accumulators (column pairs)
     if constexpr (C::RES_TMEM) {
-      // This thread's row, columns half*D/2 .. +D/2, of Q (slot 0) and u_q (slot 2):
-      // 16-bit pairs in memory are already the packed TMEM operand format.
+      // This thread's row, columns half*D/2 .. +D/2, of every operand kept in
+      // TMEM: 16-bit pairs in memory are already the packed operand format.
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int slot = t == 0 ? 0 : 2;
+      for (int slot = 0; slot < 3; ++slot) {
+        if (!in_tmem(slot)) continue;
         uint32_t w[D / 4];
         if (row < T) {
           const uint4* src = reinterpret_cast<const uint4*>(
@@ -313,7 +335,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
 #pragma unroll
           for (int v = 0; v < D / 4; ++v) w[v] = 0u;
         }
-        const uint32_t dst = (t == 0 ? tQ : tUQ) + lane_off + half * (D / 4);
+        const uint32_t dst = (slot == 0 ? tQ : (slot == 1 ? tDO : tUQ)) + lane_off + half * (D / 4);
 #pragma unroll
         for (int c16 = 0; c16 < D / 4; c16 += 16) tmem_st16_raw(dst + c16, *reinterpret_cast<uint32_t(*)[16]>(w + c16));
       }
@@ -347,28 +369,33 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       const int j0 = n * BN + c0;
       const bool need_mask = (n * BN + BN > T) || (CAUSAL && n * BN + BN - 1 > q0);
 #pragma unroll
-      for (int e = 0; e < CPW; ++e) {
-        float pr = fast_exp2(fmaf(sv[e], c, -lse));
+      for (int e = 0; e < CPW; e += 2) {
+        float x0, x1;
+        split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), LSE2), x0, x1);
+        float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
         if (need_mask) {
           const int j = j0 + e;
-          pr = ((j < T) && (!CAUSAL || j <= row)) ? pr : 0.f;
+          p0 = ((j < T) && (!CAUSAL || j <= row)) ? p0 : 0.f;
+          p1 = ((j + 1 < T) && (!CAUSAL || j + 1 <= row)) ? p1 : 0.f;
         }
+        const F2 PR = f2(p0, p1), DP = f2(dp[e], dp[e + 1]);
         if constexpr (KIND == kBwdQ) {
-          sv[e] = pr * (dp[e] - del);
+          split(mul2(PR, sub2(DP, DEL2)), sv[e], sv[e + 1]);
         } else if constexpr (KIND == kStats) {
-          const float t = pr * (gd[e] * scale);
-          a_g += t;
-          a2 = fmaf(t, dp[e], a2);
-          a4 = fmaf(pr, dp[e], a4);
-          a3 = fmaf(pr, uv[e], a3);
+          const F2 TT = mul2(PR, mul2(f2(gd[e], gd[e + 1]), SC2));
+          AG = add2(AG, TT);
+          A2 = fma2(TT, DP, A2);
+          A4 = fma2(PR, DP, A4);
+          A3 = fma2(PR, f2(uv[e], uv[e + 1]), A3);
         } else {
-          const float dpm = dp[e] - del;
-          const float gds = gd[e] * scale;
-          const float gP = fmaf(gds, dpm, fmaf(-gam, dp[e], uv[e]));
-          sv[e] = pr * dpm;          // dS
-          dp[e] = pr * (gP - rho);   // G_S
-          gd[e] = pr * (gds - gam);  // G_dP
-          uv[e] = pr;                // P
+          const F2 DPM = sub2(DP, DEL2);
+          const F2 GDS = mul2(f2(gd[e], gd[e + 1]), SC2);
+          const F2 GP = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), mul2(GAM2, DP)));
+          split(mul2(PR, DPM), sv[e], sv[e + 1]);                // dS
+          split(mul2(PR, sub2(GP, RHO2)), dp[e], dp[e + 1]);     // G_S
+          split(mul2(PR, sub2(GDS, GAM2)), gd[e], gd[e + 1]);    // G_dP
+          uv[e] = p0;                                            // P
+          uv[e + 1] = p1;
         }
       }
       if constexpr (C::NE > 0) {
@@ -391,6 +418,15 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     }
     const bool valid = row < T;
     if constexpr (KIND == kStats) {
+      float a_g, a2, a3, a4, hi_;
+      split(AG, a_g, hi_);
+      a_g += hi_;
+      split(A2, a2, hi_);
+      a2 += hi_;
+      split(A3, a3, hi_);
+      a3 += hi_;
+      split(A4, a4, hi_);
+      a4 += hi_;
       // the two column halves of each row combine through shared memory
       if (half == 1) {
         red[r * 4 + 0] = a_g;

@@ -38,9 +38,15 @@ TTT_DEV void tmem_ld32_nw(uint32_t taddr, float (&v)[32]) {
 
 template <int W>
 TTT_DEV void tmem_ld_nw(uint32_t taddr, float (&v)[W]) {
-  static_assert(W == 16 || W == 32, "");
-  if constexpr (W == 16) tmem_ld16_nw(taddr, v);
-  else tmem_ld32_nw(taddr, v);
+  static_assert(W == 16 || W == 32 || W == 64, "");
+  if constexpr (W == 16) {
+    tmem_ld16_nw(taddr, v);
+  } else if constexpr (W == 32) {
+    tmem_ld32_nw(taddr, v);
+  } else {
+    tmem_ld32_nw(taddr, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld32_nw(taddr + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+  }
 }
 
 TTT_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -53,8 +59,8 @@ TTT_DEV void reg_fence(float (&v)[N]) {
   for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
 }
 
-// Write W (16 or 32) consecutive values of row r, columns c0 .. c0+W-1 (c0 a
-// multiple of W inside one 64-column panel), into a PL(R, C) tile.
+// Write W (16, 32 or 64) consecutive values of row r, columns c0 .. c0+W-1
+// (c0 a multiple of W inside one 64-column panel), into a PL(R, C) tile.
 template <bool BF16, int W>
 TTT_DEV void store_cols(uint8_t* tile, int R, int r, int c0, const float* v) {
   uint8_t* rowp = tile + (c0 >> 6) * R * 128 + r * 128;
@@ -68,6 +74,40 @@ TTT_DEV void store_cols(uint8_t* tile, int R, int r, int c0, const float* v) {
     w.w = pack2<BF16>(v[q * 8 + 6], v[q * 8 + 7]);
     *reinterpret_cast<uint4*>(rowp + (((ch0 + q) ^ (r & 7)) << 4)) = w;
   }
+}
+
+// ---------------------------------------------------------------- packed fp32x2
+// Two independent fp32 lanes in one 64-bit register pair (sm_100a packed ops):
+// the elementwise steps work on column pairs with half the instructions.
+struct F2 {
+  unsigned long long v;
+};
+TTT_DEV F2 f2(float lo, float hi) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+  return r;
+}
+TTT_DEV F2 f2s(float x) { return f2(x, x); }
+TTT_DEV void split(F2 x, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x.v)); }
+TTT_DEV F2 add2(F2 a, F2 b) {
+  F2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+TTT_DEV F2 sub2(F2 a, F2 b) {
+  F2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+TTT_DEV F2 mul2(F2 a, F2 b) {
+  F2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+TTT_DEV F2 fma2(F2 a, F2 b, F2 c) {
+  F2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
 }
 
 // Named barrier 1 over the compute warps only (the producer and MMA warps

@@ -295,6 +295,8 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     const int cols = ttt::qm_tile_cols(pb.d, ttt::kBwdQ, false);
     TTT_TRY(encode_view(&k.str[0], a->k, pb, cols));
     TTT_TRY(encode_view(&k.str[1], a->v, pb, cols));
+    set_raw(k, 0, a->q);
+    set_raw(k, 1, a->dout);
     k.lse2 = a->lse2;
     k.delta = a->delta;
     set_out0(k, a->dq);
