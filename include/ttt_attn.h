@@ -48,7 +48,9 @@ enum ttt_status {
   TTT_ERR_TENSOR_MAP = 7,  /* the driver rejected a TMA tensor map */
   TTT_ERR_LAUNCH = 8,      /* a kernel launch failed */
   TTT_ERR_DRIVER = 9,      /* the driver entry point for tensor maps is unavailable */
-  TTT_ERR_UNSUPPORTED = 10 /* valid request this build does not implement */
+  TTT_ERR_UNSUPPORTED = 10, /* valid request this build does not implement */
+  TTT_ERR_SCRATCH = 11,     /* b*h*t_pad exceeds TTT_ATTN_NOALLOC_MAX_ROWS (ttt_attn_bwd2_noalloc) */
+  TTT_ERR_SCRATCH_SETUP = 12 /* the built-in scratch array's device address could not be obtained */
 };
 
 enum ttt_dtype { TTT_F16 = 0, TTT_BF16 = 1 };
@@ -141,6 +143,20 @@ int ttt_attn_profile_enable(int on);
  * milliseconds into counts[k] / total_ms[k] for k < n_kinds, and clears the
  * record. */
 int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds);
+
+/* Allocation-free double backward (no counterpart in the reference). Same
+ * arguments and results as ttt_attn_bwd2, except that a->gamma and a->rho are
+ * ignored: the two scratch rows come from a fixed array built into the library
+ * (2 * TTT_ATTN_NOALLOC_MAX_ROWS floats, 8 MiB, held by every GPU that loads
+ * the library until the process exits), so callers that may not allocate
+ * device memory during execution supply only inputs and outputs. Requires
+ * b*h*t_pad <= TTT_ATTN_NOALLOC_MAX_ROWS, else returns TTT_ERR_SCRATCH before
+ * enqueuing anything. All calls on a device share the array: calls that
+ * overlap on the GPU race. The first call on a device looks up the array's
+ * device address (with that device current) and should come before any stream
+ * capture. */
+#define TTT_ATTN_NOALLOC_MAX_ROWS (1 << 20)
+int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream);
 
 /* roundup(t, 128): the row count of every statistics array. */
 int ttt_attn_t_pad(int t);

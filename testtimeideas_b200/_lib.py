@@ -55,7 +55,9 @@ class Bwd2Args(ctypes.Structure):
 
 # Every symbol include/ttt_attn.h declares.
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
-            "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect")
+            "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect",
+            "ttt_attn_bwd2_noalloc")
+NOALLOC_MAX_ROWS = 1 << 20  # TTT_ATTN_NOALLOC_MAX_ROWS
 KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv")
 
 _lib = None
@@ -73,7 +75,7 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
             raise RuntimeError(
                 f"{p} not found: build the CUDA library first (python -m testtimeideas_b200.build)")
         lib = ctypes.CDLL(str(p))
-        for name in ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2"):
+        for name in ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_bwd2_noalloc"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.ttt_attn_t_pad.restype = ctypes.c_int
@@ -287,3 +289,23 @@ def profile_collect() -> dict:
     ms = (ctypes.c_double * n)()
     _check(load_library().ttt_attn_profile_collect(counts, ms, n))
     return {k: (int(counts[i]), float(ms[i])) for i, k in enumerate(KERNEL_KINDS)}
+
+
+def attn_bwd2_noalloc(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float, need_gdout: bool):
+    """attn_bwd2 through ttt_attn_bwd2_noalloc: the gamma/rho scratch comes from the
+    library's built-in array (b*h*t_pad <= NOALLOC_MAX_ROWS), for callers that may
+    not allocate device memory while the op runs; only outputs are allocated here."""
+    validate(q, k, v)
+    lib = load_library()
+    q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
+    uq, uk, uv = (prep(u.to(q.dtype)) for u in (uq, uk, uv))
+    with torch.cuda.device(q.device):
+        gq, gk, gv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
+        gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
+        args = Bwd2Args(problem(q, causal, scale), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
+                        delta.data_ptr(), view(uq), view(uk), view(uv), None, None,
+                        view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr())
+        _check(lib.ttt_attn_bwd2_noalloc(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(q.device)
+    return gq, gk, gv, gdout

@@ -207,6 +207,8 @@ const char* ttt_attn_status_string(int s) {
     case TTT_ERR_LAUNCH: return "kernel launch failed";
     case TTT_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable";
     case TTT_ERR_UNSUPPORTED: return "unsupported request";
+    case TTT_ERR_SCRATCH: return "b*h*t_pad exceeds the fixed scratch of the allocation-free entry point";
+    case TTT_ERR_SCRATCH_SETUP: return "could not obtain the device address of the built-in scratch array";
     default: return "unknown status";
   }
 }
