@@ -34,6 +34,7 @@ import subprocess
 import sys
 import time
 from pathlib import Path
+from typing import Optional
 
 import torch
 
@@ -138,14 +139,11 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- the step
-def make_inputs(cfg: dict, heads: int, rank: int, device: torch.device, seed: int = 1234) -> dict:
+def make_inputs(cfg: dict, heads: range, device: torch.device, seed: int = 1234) -> dict:
+    """Inputs of the given global heads; a head's values do not depend on the sharding."""
+    from testtimeideas_b200.sharding import head_inputs
     dtype = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
-    g = torch.Generator(device=device)
-    g.manual_seed(seed + 7919 * rank)
-    shape = (1, heads, cfg["t"], cfg["d"])
-    names = ("q", "k", "v", "do", "uq", "uk", "uv")
-    return {n: (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * cfg["scale_in"]).to(dtype)
-            for n in names}
+    return head_inputs(heads, cfg["t"], cfg["d"], dtype, device, seed=seed, scale_in=cfg["scale_in"])
 
 
 def gradgrad_step(x: dict, causal: bool):
@@ -200,8 +198,24 @@ def run_reference(args, cfg: dict) -> None:
 
 
 # ---------------------------------------------------------------- our arm
+def verify_sharded(cfg: dict, results, total_heads: int, device: torch.device) -> Optional[dict]:
+    """Gather every rank's grad-grads to rank 0 and compare them with rank 0 running
+    all heads alone (same kernels, same per-head inputs): the sharded job must give
+    bit-identical results. Returns the summary on rank 0, None elsewhere."""
+    from testtimeideas_b200.sharding import gather_heads
+    full = [gather_heads(r, total_heads) for r in results]
+    if full[0] is None:
+        return None
+    ref = gradgrad_step(make_inputs(cfg, range(total_heads), device), cfg["causal"])
+    diffs = [float((a.float() - b.float()).abs().max()) for a, b in zip(full, ref)]
+    return {"heads": total_heads, "max_abs_diff": max(diffs),
+            "bit_identical": all(torch.equal(a, b) for a, b in zip(full, ref)),
+            "against": "rank 0 running every head alone"}
+
+
 def run_ours(args, cfg: dict) -> None:
     from testtimeideas_b200 import _lib
+    from testtimeideas_b200.sharding import head_range, max_over_ranks as _max_over_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -219,7 +233,8 @@ def run_ours(args, cfg: dict) -> None:
     total_heads = cfg["b"] * cfg["h"]
     if total_heads % world:
         raise SystemExit(f"{total_heads} heads do not split over {world} GPUs")
-    heads = total_heads // world
+    mine = head_range(total_heads, world, rank)
+    heads = len(mine)
     _lib.load_library()
 
     def barrier():
@@ -227,13 +242,9 @@ def run_ours(args, cfg: dict) -> None:
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(x, device=device)
 
-    x = make_inputs(cfg, heads, rank, device)
+    x = make_inputs(cfg, mine, device)
     for _ in range(args.warmup):
         gradgrad_step(x, cfg["causal"])
     _lib.check_device_errors(device)
@@ -247,7 +258,7 @@ def run_ours(args, cfg: dict) -> None:
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
-        gradgrad_step(x, cfg["causal"])
+        last = gradgrad_step(x, cfg["causal"])
     stop.record()
     torch.cuda.synchronize(device)
     _lib.profile_enable(False)
@@ -302,6 +313,13 @@ def run_ours(args, cfg: dict) -> None:
     gpu_launches = sum(v[0] for v in prof.values())
     kernel_ms = {k: v[1] / args.steps for k, v in kern.items()}
 
+    verify = None
+    if args.verify:
+        barrier()
+        verify = verify_sharded(cfg, last, total_heads, device)
+        barrier()
+    del last
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, args.cpu_t, reps=1)
@@ -325,6 +343,8 @@ def run_ours(args, cfg: dict) -> None:
             "gpu_launches": gpu_launches,
             "kernel_ms_per_step": kernel_ms,
         }
+        if verify is not None:
+            line["verify"] = verify
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -341,6 +361,9 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-t", type=int, default=4096, help="T of the one-head CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--verify", action="store_true",
+                    help="gather the last step's grad-grads to rank 0 and check them against rank 0 running "
+                         "every head alone (untimed)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
