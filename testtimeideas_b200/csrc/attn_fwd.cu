@@ -6,7 +6,11 @@
 // _attn_fwd_kernel_stats, _attn_probs_kernel) and the PyTorch math forward of
 // the save_p modes (triton_attention.py:51-59, 270-273).
 //
-// One CTA owns 128 query rows of one head and streams 128-key tiles:
+// Two kernels: attn_fwd2_kernel (below, two query tiles per CTA, P kept in
+// tensor memory) computes O and lse2; attn_fwd_kernel (this one) is used only
+// when the normalized P is also materialized (save_p modes).
+//
+// attn_fwd_kernel: one CTA owns 128 query rows of one head and streams 128-key tiles:
 //   warp 5      TMA producer: Q once, then K/V tiles into a 2-stage ring.
 //   warp 4      MMA issuer:   S_n = Q K_n^T into TMEM (double buffered), then
 //                             O += P_n V_n into a TMEM accumulator.
@@ -20,6 +24,7 @@
 // save_p: after the main loop the CTA recomputes S for each visible tile and
 // writes the normalized P (16-bit, row-major [T, T] per head) to HBM.
 #include "attn_common.cuh"
+#include "attn_pipe.cuh"
 #include "kernels.h"
 
 namespace ttt {
@@ -290,8 +295,295 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------- two-tile forward
+// The kernel used when P is not materialized. One CTA owns 256 query rows of
+// one head as two 128-row query tiles, each with its own softmax warpgroup, and
+// streams 128-key tiles through a TMA ring:
+//   warp 9      TMA producer: Q0, Q1 once, then K_n and V_n (separate barriers,
+//                             so S can start before V lands).
+//   warp 8      MMA issuer:   S0_0, S1_0, then per key tile n:
+//                             O0 += P0_n V_n, S0_{n+1}, O1 += P1_n V_n, S1_{n+1}.
+//                             While one warpgroup exponentiates tile n the
+//                             tensor core works on the other query tile.
+//   warps 0..3  softmax of Q0, warps 4..7 softmax of Q1 (thread = query row =
+//                             TMEM lane): reads S_n, keeps the running max and
+//                             sum, writes 16-bit P_n back over the first 64
+//                             columns of S_n (packed pairs), and rescales its O
+//                             row only when the running max grew by more than
+//                             2^8.
+// P_n is the A operand of its P V product straight from tensor memory; the
+// next S product of the same query tile overwrites those columns, which is
+// safe because one thread issues both and tcgen05.mma executes in issue order.
+// By the time S_{n+1} is complete, O += P_n V_n has completed as well, so a
+// warpgroup that has seen S_{n+1} may rescale O without a further wait.
+// TMEM: S0 at columns 0..127, S1 at 128..255, O0 at 256, O1 at 256 + D.
+template <int D>
+struct Fwd2Cfg {
+  static constexpr int BM = 128, BN = 128, NQ = 2;
+  static constexpr int TILE_Q = BM * D * 2;
+  static constexpr int TILE_KV = BN * D * 2;
+  static constexpr int NSTAGE = D == 64 ? 4 : 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + NQ * TILE_Q;
+  static constexpr int OFF_V = OFF_K + NSTAGE * TILE_KV;
+  static constexpr int OFF_BAR = OFF_V + NSTAGE * TILE_KV;
+  // barrier slots: q_full, k_full[NSTAGE], v_full[NSTAGE], kv_empty[NSTAGE],
+  // s_full[2], p_full[2], pv_done[2], drain
+  static constexpr int B_Q = 0, B_K = 1, B_V = 1 + NSTAGE, B_E = 1 + 2 * NSTAGE, B_S = 1 + 3 * NSTAGE;
+  static constexpr int B_P = B_S + 2, B_O = B_P + 2, B_DR = B_O + 2, NBAR = B_DR + 1;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int NTHREADS = 320;
+  static_assert(SMEM <= 232448, "two-tile forward exceeds shared memory");
+};
+
+template <int D, bool BF16, bool CAUSAL>
+__global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant__ KParams p) {
+  using C = Fwd2Cfg<D>;
+  constexpr int BM = C::BM, BN = C::BN, NP = D / 64, NS = C::NSTAGE;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + C::B_Q;
+  uint64_t* k_full = bars + C::B_K;
+  uint64_t* v_full = bars + C::B_V;
+  uint64_t* kv_empty = bars + C::B_E;
+  uint64_t* s_full = bars + C::B_S;
+  uint64_t* p_full = bars + C::B_P;
+  uint64_t* pv_done = bars + C::B_O;
+  uint64_t* drain = bars + C::B_DR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int bidx = bh / p.H, hidx = bh % p.H;
+  const int blk = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.y;  // longest rows first
+  const int q0 = blk * 2 * BM;
+  const int T = p.T;
+  const int n_all = (T + BN - 1) / BN;
+  // key tiles visited by query tile w (none when the tile starts past the sequence)
+  const int qs0 = q0, qs1 = q0 + BM;
+  const int nt0 = qs0 >= T ? 0 : (CAUSAL ? min(n_all, qs0 / BN + 1) : n_all);
+  const int nt1 = qs1 >= T ? 0 : (CAUSAL ? min(n_all, qs1 / BN + 1) : n_all);
+  const int n_kv = max(nt0, nt1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NBAR; ++i) mbar_init(bars + i, 1);
+    mbar_init(p_full + 0, 128);
+    mbar_init(p_full + 1, 128);
+    *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (*abort_flag) return;
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  Guard g{abort_flag, p.err};
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch(&p.own[0]);
+      tma_prefetch(&p.str[0]);
+      tma_prefetch(&p.str[1]);
+      mbar_arrive_tx(q_full, (nt1 > 0 ? 2 : 1) * C::TILE_Q);
+      for (int pp = 0; pp < NP; ++pp) tma_load_4d(sQ + pp * BM * 128, &p.own[0], q_full, pp * 64, qs0, hidx, bidx);
+      if (nt1 > 0)
+        for (int pp = 0; pp < NP; ++pp)
+          tma_load_4d(sQ + C::TILE_Q + pp * BM * 128, &p.own[0], q_full, pp * 64, qs1, hidx, bidx);
+      int n = 0;
+      for (; n < n_kv; ++n) {
+        const int s = n % NS;
+        if (n >= NS && !mbar_wait(kv_empty + s, ((n / NS) - 1) & 1, g, 1)) break;
+        mbar_arrive_tx(k_full + s, C::TILE_KV);
+        for (int pp = 0; pp < NP; ++pp)
+          tma_load_4d(sK + s * C::TILE_KV + pp * BN * 128, &p.str[0], k_full + s, pp * 64, n * BN, hidx, bidx);
+        mbar_arrive_tx(v_full + s, C::TILE_KV);
+        for (int pp = 0; pp < NP; ++pp)
+          tma_load_4d(sV + s * C::TILE_KV + pp * BN * 128, &p.str[1], v_full + s, pp * 64, n * BN, hidx, bidx);
+      }
+      // Wait for every load this thread issued before the CTA may exit.
+      mbar_drain(q_full, 0);
+      for (int j = max(0, n - NS); j < n; ++j) {
+        mbar_drain(k_full + j % NS, (j / NS) & 1);
+        mbar_drain(v_full + j % NS, (j / NS) & 1);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(128, BN, BF16, false, false);
+      constexpr uint32_t id_o = idesc_f16(128, D, BF16, false, true);
+      const int nt[2] = {nt0, nt1};
+      int k_seen = 0;  // key tiles whose K load this thread has waited for
+      bool ok = mbar_wait(q_full, 0, g, 2);
+      auto wait_k = [&](int n) -> bool {
+        if (n < k_seen) return true;
+        if (!mbar_wait(k_full + n % NS, (n / NS) & 1, g, 3)) return false;
+        k_seen = n + 1;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_s = [&](int w, int n) {
+        const uint32_t aq = smem_u32(sQ + w * C::TILE_Q), bk = smem_u32(sK + (n % NS) * C::TILE_KV);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + w * 128, desc_kmajor(aq, BM, kk), desc_kmajor(bk, BN, kk), id_s, kk > 0 ? 1u : 0u);
+        umma_commit(s_full + w);
+      };
+      if (ok && n_kv > 0 && (ok = wait_k(0))) {
+        if (nt0 > 0) issue_s(0, 0);
+        if (nt1 > 0) issue_s(1, 0);
+      }
+      for (int n = 0; ok && n < n_kv; ++n) {
+        const int s = n % NS;
+        if (!(ok = mbar_wait(v_full + s, (n / NS) & 1, g, 4))) break;
+        const uint32_t bv = smem_u32(sV + s * C::TILE_KV);
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (n >= nt[w]) continue;
+          if (!(ok = mbar_wait(p_full + w, n & 1, g, 5))) break;
+          tc_fence_after();
+          const uint32_t tP = tmem + w * 128, tO = tmem + 256 + w * D;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            umma_ts(tO, tP + kk * 8, desc_mnmajor(bv, BN, kk), id_o, (n > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(pv_done + w);
+          if (n + 1 < nt[w]) {
+            if (!(ok = wait_k(n + 1))) break;
+            issue_s(w, n + 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(kv_empty + s);
+      }
+      // Drain: every tcgen05 op issued above must finish before TMEM is freed.
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps 0..7
+    const int w = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int row = q0 + w * BM + r;
+    const int ntw = w ? nt1 : nt0;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_off + w * 128;
+    const uint32_t tO = tmem + lane_off + 256 + w * D;
+    const float c = p.scale_log2;
+    const int qw0 = q0 + w * BM;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int n = 0; n < ntw; ++n) {
+      if (!mbar_wait(s_full + w, n & 1, g, 6)) { ok = false; break; }
+      tc_fence_after();
+      float sv[BN];
+      tmem_ld_nw<64>(tS, *reinterpret_cast<float(*)[64]>(sv));
+      tmem_ld_nw<64>(tS + 64, *reinterpret_cast<float(*)[64]>(sv + 64));
+      tmem_wait_ld();
+      reg_fence(sv);
+      const int k0 = n * BN;
+      if ((k0 + BN > T) || (CAUSAL && k0 + BN - 1 > qw0)) {
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int col = k0 + j;
+          sv[j] = ((col < T) && (!CAUSAL || col <= row)) ? sv[j] : -INFINITY;
+        }
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int j = 8; j < BN; ++j) mx8[j & 7] = fmaxf(mx8[j & 7], sv[j]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m_used, mx * c);
+      if (n == 0) {
+        m_used = m_new;
+      } else {
+        const bool need = m_new > m_used + 8.f;
+        if (__any_sync(0xffffffffu, need)) {
+          // O += P_{n-1} V_{n-1} completed before S_n did (issue order), so O is settled.
+          const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
+          if (need) {
+            l *= alpha;
+            m_used = m_new;
+          }
+#pragma unroll
+          for (int q = 0; q < D / 16; ++q) {
+            float o[16];
+            tmem_ld16(tO + q * 16, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tmem_st16(tO + q * 16, o);
+          }
+        }
+      }
+      const F2 C2 = f2s(c), NM = f2s(-m_used);
+      F2 acc[4] = {f2s(0.f), f2s(0.f), f2s(0.f), f2s(0.f)};
+#pragma unroll
+      for (int q = 0; q < BN / 32; ++q) {
+        uint32_t pw[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int e = q * 32 + 2 * j;
+          float x0, x1;
+          split(fma2(f2(sv[e], sv[e + 1]), C2, NM), x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          acc[j & 3] = add2(acc[j & 3], f2(p0, p1));
+          pw[j] = pack2<BF16>(p0, p1);
+        }
+        tmem_st16_raw(tS + q * 16, pw);
+      }
+      float a0, a1;
+      split(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), a0, a1);
+      l += a0 + a1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full + w);
+    }
+    if (ok && ntw > 0) {
+      if (mbar_wait(pv_done + w, (ntw - 1) & 1, g, 9)) {
+        tc_fence_after();
+        const bool valid = row < T;
+        uint16_t* orow = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
+                         static_cast<int64_t>(row) * p.o0_st;
+        acc_to_global<D, BF16>(tO, orow, valid, 1.f / l);
+        if (row < p.t_pad) p.out_f0[static_cast<int64_t>(bh) * p.t_pad + row] = valid ? m_used + __log2f(l) : INFINITY;
+      }
+    } else if (ok && row < p.t_pad) {
+      p.out_f0[static_cast<int64_t>(bh) * p.t_pad + row] = INFINITY;  // pad rows of a tile past the sequence
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+template <int D, bool BF16, bool CAUSAL>
+static cudaError_t launch_fwd2_t(const KParams& p, cudaStream_t stream) {
+  using C = Fwd2Cfg<D>;
+  auto kern = attn_fwd2_kernel<D, BF16, CAUSAL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.B * p.H, (p.T + 2 * C::BM - 1) / (2 * C::BM));
+  kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(p);
+  return cudaGetLastError();
+}
+
 template <int D, bool BF16, bool CAUSAL, bool SAVE_P>
 static cudaError_t launch_fwd_t(const KParams& p, cudaStream_t stream) {
+  if constexpr (!SAVE_P) return launch_fwd2_t<D, BF16, CAUSAL>(p, stream);
   using C = FwdCfg<D, SAVE_P>;
   auto kern = attn_fwd_kernel<D, BF16, CAUSAL, SAVE_P>;
   static bool configured = false;  // per-instantiation; attribute is per-device but idempotent
