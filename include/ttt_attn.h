@@ -122,6 +122,35 @@ typedef struct {
 } ttt_bwd2_args;
 int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream);
 
+/* Passes over materialized probabilities. p is P = softmax(scale * q k^T
+ * [causal mask]) as a [b, h, t, t] 16-bit view (same dtype as the other
+ * tensors): p.sb, p.sh are the head strides and p.st the row stride, all
+ * positive multiples of 8 elements with p.st >= t; entries are read as
+ * given. rowsum arrays are fp32 [b*h, t], contiguous. pb.d, pb.dtype as
+ * elsewhere; pb.causal: tiles entirely past the diagonal are skipped (the
+ * entries there are taken to be zero); pb.scale as in the forward. */
+typedef struct {
+  ttt_problem pb;
+  ttt_view p;
+  ttt_view q, k, v, dout;
+  const float* rowsum; /* input of ttt_attn_dqdk_from_p */
+  float* rowsum_out;   /* output of ttt_attn_rowsum_from_p */
+  ttt_view dq, dk, dv;
+  int32_t* err;
+} ttt_from_p_args;
+/* dv = P^T dout (reads all of P; pb.causal and pb.scale are ignored).
+ * Replaces: backward_stubs.py:124-181 (_attn_bwd_dv_from_p_kernel,
+ * triton_attn_bwd_dv_from_p). */
+int ttt_attn_dv_from_p(const ttt_from_p_args* a, void* stream);
+/* rowsum_out[bh, i] = sum_j P_ij (dout_i . v_j).
+ * Replaces: backward_stubs.py:184-255 (_attn_rowsum_kernel,
+ * triton_attn_rowsum_from_p). */
+int ttt_attn_rowsum_from_p(const ttt_from_p_args* a, void* stream);
+/* dq = scale * dS k, dk = scale * dS^T q with dS = P o (dout v^T - rowsum).
+ * Replaces: backward_stubs.py:259-425 (_attn_bwd_dq_kernel,
+ * _attn_bwd_dk_kernel, triton_attn_bwd_dqdk_from_p). */
+int ttt_attn_dqdk_from_p(const ttt_from_p_args* a, void* stream);
+
 /* Kernel kinds reported by the profiling hook. */
 enum ttt_kernel_kind {
   TTT_K_FWD = 0,         /* forward (O, lse2 [, P]) */
@@ -131,7 +160,8 @@ enum ttt_kernel_kind {
   TTT_K_BWD2_STATS = 4,  /* gamma, rho row statistics */
   TTT_K_BWD2_Q = 5,      /* dd_q (+ dd_dout) */
   TTT_K_BWD2_KV = 6,     /* dd_k, dd_v */
-  TTT_K_COUNT = 7
+  TTT_K_FROM_P = 7,      /* passes over materialized P */
+  TTT_K_COUNT = 8
 };
 
 /* Profiling hook (no reference counterpart; the reference times whole steps

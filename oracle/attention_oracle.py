@@ -126,6 +126,53 @@ def closed_form_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | N
             "delta": delta[..., 0], "gamma": gamma[..., 0], "rho": rho[..., 0]}
 
 
+# ---------------------------------------------------------------- passes over a given P
+# Restatements of the reference's P-taking helpers (backward_stubs.py), numpy
+# float64 on [b, h, t, t] P and [b, h, t, d] tensors. ``causal`` follows the
+# reference's block skip: a 64 x 64 block of P is used only if its last query
+# row is at or past its first key column (backward_stubs.py:212-215, 291-294,
+# 336-337); inside a used block P is taken as given.
+_BLOCK = 64
+
+
+def _causal_block_mask(t: int) -> np.ndarray:
+    """[t, t] 0/1 mask of the (query, key) entries inside blocks the reference visits."""
+    i = np.arange(t)
+    last_q = (i // _BLOCK) * _BLOCK + _BLOCK - 1          # last query row of each query block
+    first_k = (i // _BLOCK) * _BLOCK                      # first key of each key block
+    return (last_q[:, None] >= first_k[None, :]).astype(np.float64)
+
+
+def dv_from_p(p, do):
+    """dV = P^T dO  (backward_stubs.py:124-181)."""
+    p64, do64 = _np64(p), _np64(do)
+    return np.einsum("bhqk,bhqd->bhkd", p64, do64)
+
+
+def rowsum_from_p(p, do, v, causal: bool):
+    """rowsum_i = sum_j P_ij (dO_i . V_j)  (backward_stubs.py:184-255)."""
+    p64, do64, v64 = _np64(p), _np64(do), _np64(v)
+    if causal:
+        p64 = p64 * _causal_block_mask(p64.shape[-1])
+    dp = np.einsum("bhqd,bhkd->bhqk", do64, v64)
+    return (dp * p64).sum(-1)
+
+
+def dqdk_from_p(q, k, v, do, p, rowsum, causal: bool, scale: float):
+    """dS = (dO V^T - rowsum) o P; dQ = scale dS K; dK = scale dS^T Q  (backward_stubs.py:259-425)."""
+    q64, k64, v64, do64, p64, rs64 = (_np64(x) for x in (q, k, v, do, p, rowsum))
+    if causal:
+        p64 = p64 * _causal_block_mask(p64.shape[-1])
+    ds = (np.einsum("bhqd,bhkd->bhqk", do64, v64) - rs64[..., None]) * p64
+    return scale * np.einsum("bhqk,bhkd->bhqd", ds, k64), scale * np.einsum("bhqk,bhqd->bhkd", ds, q64)
+
+
+def _np64(x):
+    if isinstance(x, torch.Tensor):
+        return x.detach().to("cpu", torch.float64).numpy()
+    return np.asarray(x, dtype=np.float64)
+
+
 def seeded_inputs(b: int, h: int, t: int, d: int, seed: int, scale_in: float = 1.0,
                   dtype: torch.dtype = torch.float32) -> dict:
     """q, k, v, do, uq, uk, uv iid N(0,1) * scale_in from one CPU generator

@@ -9,7 +9,9 @@ the reference runs its math path (triton_attention.py:275-280 forward,
 416-420 recompute backward). Outputs: forward O, first-order grads of
 <O, dO> (create_graph=True) and second-order grads of <dq,uq>+<dk,uk>+<dv,uv>.
 
-Also records the reference's ``save_p`` mode on the same inputs; its
+Also records the backward methods of the reference's P-taking autograd
+Functions (TritonDvFn, TritonRowSumFn, TritonDqDkFn) on fixed inputs, and the
+reference's ``save_p`` mode on the same inputs as the math path; its
 grad-grad for q and k differs from the math path because P is saved as a
 constant (backward_stubs.py:428-514); the tests pin that difference too.
 
@@ -71,8 +73,51 @@ def run_reference_mean_loss(ta, inputs, causal):
     return {"gq": gg[0], "gk": gg[1], "gv": gg[2]}
 
 
+class _Ctx:
+    """Stand-in for an autograd context: just the saved tensors and attributes."""
+
+    def __init__(self, saved, **attrs):
+        self.saved_tensors = saved
+        self.__dict__.update(attrs)
+
+
+def from_p_function_backwards(out_path: Path) -> None:
+    """Outputs of the backward methods of the reference's TritonDvFn,
+    TritonRowSumFn and TritonDqDkFn (backward_stubs.py:428-514). Those methods
+    are plain torch code, so they run on CPU with a stand-in context; their
+    forwards are Triton kernels and are not run here."""
+    bs = sys.modules["ref_ttt_kernels.backward_stubs"]
+    b, h, t, d, causal = 1, 2, 48, 16, True
+    scale = 1.0 / math.sqrt(d)
+    g = torch.Generator().manual_seed(17)
+    rnd = lambda *shape: torch.randn(*shape, generator=g, dtype=torch.float64)  # noqa: E731
+    q, k, v, do = (rnd(b, h, t, d) for _ in range(4))
+    s = torch.matmul(q, k.transpose(-2, -1)) * scale
+    s = s.masked_fill(torch.triu(torch.ones(t, t, dtype=torch.bool), 1), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    rowsum = (torch.matmul(do, v.transpose(-2, -1)) * p).sum(-1)
+    gdv, gdq, gdk = rnd(b, h, t, d), rnd(b, h, t, d), rnd(b, h, t, d)
+    grs = rnd(b, h, t)
+    rec = {"q": q, "k": k, "v": v, "do": do, "p": p, "rowsum": rowsum, "gdv": gdv, "gdq": gdq, "gdk": gdk,
+           "grs": grs}
+    out = bs.TritonDvFn.backward(_Ctx((p, do)), gdv)
+    rec.update({"dvfn_grad_p": out[0], "dvfn_grad_do": out[1]})
+    out = bs.TritonRowSumFn.backward(_Ctx((p, do, v), causal=causal), grs)
+    rec.update({"rsfn_grad_p": out[0], "rsfn_grad_do": out[1], "rsfn_grad_v": out[2]})
+    out = bs.TritonDqDkFn.backward(_Ctx((q, k, v, do, p, rowsum), scale=scale, causal=causal), gdq, gdk)
+    for name, x in zip(("q", "k", "v", "do", "p", "rowsum"), out[:6]):
+        rec[f"dqdkfn_grad_{name}"] = x
+    rec = {n: x.detach().numpy() for n, x in rec.items()}
+    rec["meta"] = np.array([b, h, t, d, int(causal)], dtype=np.int64)
+    rec["scale"] = np.array(scale)
+    np.savez_compressed(out_path, **rec)
+    print(f"wrote {out_path.name}")
+
+
 def main() -> None:
     ta = load_reference()
+    importlib.import_module("ref_ttt_kernels.backward_stubs")
+    from_p_function_backwards(HERE / "from_p_function_backwards_t48_d16_fp64.npz")
     for name, b, h, t, d, causal, dtype, seed, sc in CASES:
         g = torch.Generator().manual_seed(seed)
         inputs = {n: (torch.randn(b, h, t, d, generator=g, dtype=torch.float64) * sc).to(dtype)

@@ -17,7 +17,9 @@ import torch
 
 from oracle import attention_oracle as orc
 
-GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+# attention-path cases (the P-taking Function fixture is covered by test_from_p_cpu.py)
+GOLDEN = sorted(p for p in glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz"))
+                if not os.path.basename(p).startswith("from_p_"))
 NAMES = ("q", "k", "v", "do", "uq", "uk", "uv")
 
 

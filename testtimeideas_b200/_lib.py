@@ -53,12 +53,18 @@ class Bwd2Args(ctypes.Structure):
                 ("gq", View), ("gk", View), ("gv", View), ("gdout", View), ("err", ctypes.c_void_p)]
 
 
+class FromPArgs(ctypes.Structure):
+    _fields_ = [("pb", Problem), ("p", View), ("q", View), ("k", View), ("v", View), ("dout", View),
+                ("rowsum", ctypes.c_void_p), ("rowsum_out", ctypes.c_void_p),
+                ("dq", View), ("dk", View), ("dv", View), ("err", ctypes.c_void_p)]
+
+
 # Every symbol include/ttt_attn.h declares.
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
             "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect",
-            "ttt_attn_bwd2_noalloc")
+            "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p", "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p")
 NOALLOC_MAX_ROWS = 1 << 20  # TTT_ATTN_NOALLOC_MAX_ROWS
-KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv")
+KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv", "from_p")
 
 _lib = None
 _lib_lock = threading.Lock()
@@ -75,7 +81,8 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
             raise RuntimeError(
                 f"{p} not found: build the CUDA library first (python -m testtimeideas_b200.build)")
         lib = ctypes.CDLL(str(p))
-        for name in ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_bwd2_noalloc"):
+        for name in ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p",
+                     "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p"):
             getattr(lib, name).restype = ctypes.c_int
             getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.ttt_attn_t_pad.restype = ctypes.c_int
@@ -204,7 +211,8 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False):
     with torch.cuda.device(q.device):
         o = torch.empty((b, h, t, d), dtype=q.dtype, device=q.device)
         lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
-        p = torch.empty((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
+        # causal: the kernel writes only key tiles up to the diagonal; the rest stays zero
+        p = (torch.zeros if causal else torch.empty)((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
         args = FwdArgs(problem(q, causal, scale), view(q), view(k), view(v), view(o), lse2.data_ptr(),
                        p.data_ptr() if p is not None else None, error_word(q.device).data_ptr())
         _check(lib.ttt_attn_fwd(ctypes.byref(args), _stream()))
@@ -309,3 +317,97 @@ def attn_bwd2_noalloc(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scal
         if _SYNC_CHECK:
             check_device_errors(q.device)
     return gq, gk, gv, gdout
+
+
+# ---------------------------------------------------------------- passes over materialized P
+def prep_p(p: torch.Tensor) -> torch.Tensor:
+    """P as a [b, h, t, t] view TMA can read: unit column stride, 16-byte aligned
+    base, row and head strides multiples of 8 elements. Otherwise copied into a
+    zero-padded buffer whose rows are rounded up to 8 elements."""
+    if p.dim() != 4 or p.shape[-1] != p.shape[-2]:
+        raise ValueError(f"expected P as [b, h, t, t], got shape {tuple(p.shape)}")
+    b, h, t, _ = p.shape
+    ok = p.stride(3) == 1 and p.data_ptr() % 16 == 0 and p.stride(2) >= t and p.stride(2) % 8 == 0
+    for size, stride in ((b, p.stride(0)), (h, p.stride(1))):
+        if size > 1 and (stride <= 0 or stride % 8 != 0):
+            ok = False
+    if ok:
+        return p
+    tp = (t + 7) // 8 * 8
+    buf = torch.zeros((b, h, t, tp), dtype=p.dtype, device=p.device)
+    buf[..., :t].copy_(p)
+    return buf[..., :t]
+
+
+def _from_p_check(p: torch.Tensor, *xs: torch.Tensor) -> None:
+    if not p.is_cuda or any(not x.is_cuda for x in xs):
+        raise ValueError("ttt attention kernels need CUDA tensors")
+    ref = xs[0]
+    _dtype_code(ref)
+    if ref.shape[-1] not in (64, 128):
+        raise ValueError(f"head dim must be 64 or 128, got {ref.shape[-1]}")
+    for x in xs:
+        if x.shape != ref.shape or x.dtype != ref.dtype:
+            raise ValueError("the [b, h, t, d] operands must share one shape and dtype")
+    b, h, t, _ = ref.shape
+    if tuple(p.shape) != (b, h, t, t):
+        raise ValueError(f"P must be [b, h, t, t] = {(b, h, t, t)}, got {tuple(p.shape)}")
+
+
+def _from_p_args(p, ref, causal: bool, scale: float, **views) -> FromPArgs:
+    a = FromPArgs()
+    a.pb = problem(ref, causal, scale)
+    a.p = view(p)
+    for name, x in views.items():
+        if isinstance(x, torch.Tensor) and x.dtype == torch.float32 and x.dim() == 2:
+            setattr(a, name, x.data_ptr())
+        else:
+            setattr(a, name, view(x))
+    a.err = error_word(ref.device).data_ptr()
+    return a
+
+
+def dv_from_p(p: torch.Tensor, dout: torch.Tensor) -> torch.Tensor:
+    """dV = P^T dout for P [b, h, t, t] and dout [b, h, t, d] (every entry of P is read)."""
+    _from_p_check(p, dout)
+    lib = load_library()
+    p, dout = prep_p(p.to(dout.dtype)), prep(dout)
+    with torch.cuda.device(dout.device):
+        dv = torch.empty_like(dout, memory_format=torch.contiguous_format)
+        args = _from_p_args(p, dout, False, 1.0, dout=dout, dv=dv)
+        _check(lib.ttt_attn_dv_from_p(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(dout.device)
+    return dv
+
+
+def rowsum_from_p(p: torch.Tensor, dout: torch.Tensor, v: torch.Tensor, causal: bool) -> torch.Tensor:
+    """rowsum[b, h, i] = sum_j P_ij (dout_i . v_j), fp32 [b, h, t]."""
+    _from_p_check(p, dout, v)
+    lib = load_library()
+    p, dout, v = prep_p(p.to(dout.dtype)), prep(dout), prep(v)
+    b, h, t, _ = dout.shape
+    with torch.cuda.device(dout.device):
+        rs = torch.empty((b * h, t), dtype=torch.float32, device=dout.device)
+        args = _from_p_args(p, dout, causal, 1.0, dout=dout, v=v, rowsum_out=rs)
+        _check(lib.ttt_attn_rowsum_from_p(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(dout.device)
+    return rs.view(b, h, t)
+
+
+def dqdk_from_p(q, k, v, dout, p, rowsum, causal: bool, scale: float):
+    """dq = scale dS k, dk = scale dS^T q with dS = P o (dout v^T - rowsum)."""
+    _from_p_check(p, q, k, v, dout)
+    lib = load_library()
+    q, k, v, dout = prep(q), prep(k), prep(v), prep(dout)
+    p = prep_p(p.to(q.dtype))
+    b, h, t, _ = q.shape
+    rs = rowsum.reshape(b * h, t).to(torch.float32).contiguous()
+    with torch.cuda.device(q.device):
+        dq, dk = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(2))
+        args = _from_p_args(p, q, causal, scale, q=q, k=k, v=v, dout=dout, rowsum=rs, dq=dq, dk=dk)
+        _check(lib.ttt_attn_dqdk_from_p(ctypes.byref(args), _stream()))
+        if _SYNC_CHECK:
+            check_device_errors(q.device)
+    return dq, dk

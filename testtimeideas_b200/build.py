@@ -25,7 +25,7 @@ BUILD = PKG / "_build"
 LIBDIR = PKG / "_lib"
 LIB = LIBDIR / "libttt_attn.so"
 
-SOURCES = ["capi.cu", "attn_fwd.cu", "attn_bwd_qm.cu", "attn_bwd_km.cu", "misc.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "attn_fwd.cu", "attn_bwd_qm.cu", "attn_bwd_km.cu", "misc.cu", "noalloc.cu", "attn_from_p.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]

@@ -99,6 +99,40 @@ int encode_stats(CUtensorMap* m, const float* p, int bh, int t_pad, int cols) {
   return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
 }
 
+// P view [b, h, t, t]: row stride p.st >= t, head strides; all multiples of 8.
+int check_p_view(const ttt_view& v, const ttt_problem& pb) {
+  if (v.ptr == nullptr) return TTT_ERR_NULL;
+  if (!aligned16(v.ptr)) return TTT_ERR_ALIGN;
+  const int64_t s[3] = {v.sb, v.sh, v.st};
+  const int64_t n[3] = {pb.b, pb.h, pb.t};
+  for (int i = 0; i < 3; ++i) {
+    if (n[i] == 1 && i < 2) continue;
+    if (s[i] <= 0 || (s[i] % 8) != 0) return TTT_ERR_STRIDE;
+  }
+  if (v.st < pb.t) return TTT_ERR_STRIDE;
+  return TTT_OK;
+}
+
+// 4-D map over a [b, h, t, t] probability view: dims (t, t, h, b), box (64, rows, 1, 1).
+int encode_p(CUtensorMap* m, const ttt_view& v, const ttt_problem& pb, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TTT_ERR_DRIVER;
+  const int64_t st = v.st;
+  const int64_t sh = pb.h > 1 ? v.sh : st * pb.t;
+  const int64_t sb = pb.b > 1 ? v.sb : sh * pb.h;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(pb.t), static_cast<cuuint64_t>(pb.t),
+                        static_cast<cuuint64_t>(pb.h), static_cast<cuuint64_t>(pb.b)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st * 2), static_cast<cuuint64_t>(sh * 2),
+                           static_cast<cuuint64_t>(sb * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      pb.dtype == TTT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, 4, v.ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
+}
+
 void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
   k.B = pb.b;
   k.H = pb.h;
@@ -384,6 +418,85 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   {
     ProfScope prof(TTT_K_BWD2_KV, s);
     TTT_TRY(launched(ttt::launch_km(kk, pb.d, bf16, causal, ttt::kBwd2KV, s)));
+  }
+  return TTT_OK;
+}
+
+int ttt_attn_dv_from_p(const ttt_from_p_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  TTT_TRY(check_p_view(a->p, pb));
+  TTT_TRY(check_view(a->dout, pb));
+  TTT_TRY(check_view(a->dv, pb));
+  KParams k;
+  std::memset(&k, 0, sizeof(k));
+  fill_common(k, pb, a->err);
+  TTT_TRY(encode_p(&k.str[0], a->p, pb, ttt::from_p_box_rows(ttt::kFpDV)));
+  TTT_TRY(encode_view(&k.str[1], a->dout, pb, ttt::from_p_stream_rows(ttt::kFpDV)));
+  set_out0(k, a->dv);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope prof(TTT_K_FROM_P, s);
+  return launched(ttt::launch_from_p(k, pb.d, pb.dtype == TTT_BF16, false, ttt::kFpDV, s));
+}
+
+int ttt_attn_rowsum_from_p(const ttt_from_p_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  TTT_TRY(check_p_view(a->p, pb));
+  TTT_TRY(check_view(a->dout, pb));
+  TTT_TRY(check_view(a->v, pb));
+  if (a->rowsum_out == nullptr) return TTT_ERR_NULL;
+  KParams k;
+  std::memset(&k, 0, sizeof(k));
+  fill_common(k, pb, a->err);
+  TTT_TRY(encode_p(&k.str[0], a->p, pb, ttt::from_p_box_rows(ttt::kFpRowsum)));
+  TTT_TRY(encode_view(&k.str[1], a->v, pb, ttt::from_p_stream_rows(ttt::kFpRowsum)));
+  set_raw(k, 0, a->dout);
+  k.out_f0 = a->rowsum_out;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope prof(TTT_K_FROM_P, s);
+  return launched(ttt::launch_from_p(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, ttt::kFpRowsum, s));
+}
+
+int ttt_attn_dqdk_from_p(const ttt_from_p_args* a, void* stream) {
+  if (a == nullptr) return TTT_ERR_NULL;
+  const ttt_problem& pb = a->pb;
+  TTT_TRY(check_problem(pb));
+  TTT_TRY(check_p_view(a->p, pb));
+  const ttt_view* views[] = {&a->q, &a->k, &a->v, &a->dout, &a->dq, &a->dk};
+  for (const ttt_view* v : views) TTT_TRY(check_view(*v, pb));
+  if (a->rowsum == nullptr) return TTT_ERR_NULL;
+  const bool bf16 = pb.dtype == TTT_BF16, causal = pb.causal != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    // dK: key-major, V resident, P / dO / Q streamed per 64 queries
+    KParams k;
+    std::memset(&k, 0, sizeof(k));
+    fill_common(k, pb, a->err);
+    TTT_TRY(encode_view(&k.own[0], a->v, pb, 128));
+    TTT_TRY(encode_p(&k.str[0], a->p, pb, ttt::from_p_box_rows(ttt::kFpDK)));
+    TTT_TRY(encode_view(&k.str[1], a->dout, pb, ttt::from_p_stream_rows(ttt::kFpDK)));
+    TTT_TRY(encode_view(&k.str[2], a->q, pb, ttt::from_p_stream_rows(ttt::kFpDK)));
+    k.delta = a->rowsum;
+    set_out0(k, a->dk);
+    ProfScope prof(TTT_K_FROM_P, s);
+    TTT_TRY(launched(ttt::launch_from_p(k, pb.d, bf16, causal, ttt::kFpDK, s)));
+  }
+  {
+    // dQ: query-major, dO resident, P / V / K streamed per 64 keys
+    KParams k;
+    std::memset(&k, 0, sizeof(k));
+    fill_common(k, pb, a->err);
+    TTT_TRY(encode_view(&k.own[0], a->dout, pb, 128));
+    TTT_TRY(encode_p(&k.str[0], a->p, pb, ttt::from_p_box_rows(ttt::kFpDQ)));
+    TTT_TRY(encode_view(&k.str[1], a->v, pb, ttt::from_p_stream_rows(ttt::kFpDQ)));
+    TTT_TRY(encode_view(&k.str[2], a->k, pb, ttt::from_p_stream_rows(ttt::kFpDQ)));
+    k.delta = a->rowsum;
+    set_out0(k, a->dq);
+    ProfScope prof(TTT_K_FROM_P, s);
+    TTT_TRY(launched(ttt::launch_from_p(k, pb.d, bf16, causal, ttt::kFpDQ, s)));
   }
   return TTT_OK;
 }

@@ -17,6 +17,20 @@ cudaError_t launch_km(const KParams& p, int d, bool bf16, bool causal, int kind,
 int qm_tile_cols(int d, int kind, bool gdo);
 int km_tile_rows(int d, int kind);
 
+// Passes that read the materialized probabilities P ([b, h, t, t], map in
+// str[0]) instead of recomputing them.
+enum FpMode : int {
+  kFpDV = 0,      // dV = P^T dO                    (str[1] = dO)
+  kFpRowsum = 1,  // rowsum = rowsum(dO o (P V))    (str[1] = V, raw[0] = dO, out_f0 = rowsum [b*h, t])
+  kFpDK = 2,      // dK = scale dS^T Q              (own[0] = V, str[1] = dO, str[2] = Q, delta = rowsum [b*h, t])
+  kFpDQ = 3,      // dQ = scale dS K                (own[0] = dO, str[1] = V, str[2] = K, delta = rowsum [b*h, t])
+};
+// Rows of the P box each mode expects (the streamed tiles of kFpDK use 64 rows,
+// the others 128).
+inline int from_p_box_rows(int mode) { return mode == kFpDK ? 64 : 128; }
+inline int from_p_stream_rows(int mode) { return (mode == kFpDK || mode == kFpDQ) ? 64 : 128; }
+cudaError_t launch_from_p(const KParams& p, int d, bool bf16, bool causal, int mode, cudaStream_t stream);
+
 // delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t < T, 0 for T <= t < t_pad.
 struct DeltaArgs {
   const uint16_t* o;
