@@ -54,11 +54,23 @@ CONFIGS = {
                  workload="8-head slice of BASELINE config 4 (profiling size): T=16384 d=128 bf16 causal"),
     "c2": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5,
                workload="BASELINE config 2 shape: grad-grad b=2 h=4 T=2048 d=128 fp16 non-causal"),
+    # P-streaming first-order backward (the reference's save_p_triton_full data flow):
+    # forward writing P, then dv / rowsum / dq+dk from P; HBM-bound on P.
+    "c2p": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5, step="from_p", flush=True,
+                workload="BASELINE config 2: fwd (P written) + first-order backward from P "
+                         "(dv/rowsum/dq+dk from P) b=2 h=4 T=2048 d=128 fp16 non-causal"),
+    "c2pc": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=True, scale_in=0.5, step="from_p", flush=True,
+                 workload="BASELINE config 2: fwd (P written) + first-order backward from P "
+                          "(dv/rowsum/dq+dk from P) b=2 h=4 T=2048 d=128 fp16 causal"),
+    "c8p": dict(b=1, h=8, t=8192, d=128, dtype="fp16", causal=False, scale_in=0.5, step="from_p",
+                workload="fwd (P written) + first-order backward from P, b=1 h=8 T=8192 d=128 fp16 "
+                         "non-causal (P = 1 GiB, larger than L2)"),
 }
 # Algorithmic flops per head, in units of T^2 d, that each kernel kind contributes
 # (each of the 14 distinct products of the grad-grad step is assigned to the
 # kernel that first computes it; recomputed products count nowhere).
-ALGO_UNITS = {"fwd": 4, "delta": 0, "bwd_kv": 6, "bwd_q": 2, "bwd2_stats": 6, "bwd2_q": 4, "bwd2_kv": 6}
+ALGO_UNITS = {"fwd": 4, "delta": 0, "bwd_kv": 6, "bwd_q": 2, "bwd2_stats": 6, "bwd2_q": 4, "bwd2_kv": 6,
+              "from_p": 0}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -67,7 +79,22 @@ def causal_factor(t: int, causal: bool) -> float:
 
 
 def step_flops(cfg: dict, heads: int) -> float:
-    return 28.0 * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+    """Algorithmic flops of one step: 28 T^2 d per head for the grad-grad step,
+    12 T^2 d for forward + first-order backward (the from-P step)."""
+    units = 12.0 if cfg.get("step") == "from_p" else 28.0
+    return units * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+
+
+def from_p_bytes(cfg: dict, heads: int) -> float:
+    """Algorithmic HBM bytes of the four from-P launches of one step: P read by each
+    of them (the causal ones only its lower triangle), each [t, d] 16-bit operand
+    read or written once per launch, and the fp32 rowsum rows."""
+    t, d = cfg["t"], cfg["d"]
+    cf = causal_factor(t, cfg["causal"])
+    p_reads = 2.0 * t * t * (1.0 + 3.0 * cf)
+    td = 2.0 * t * d * (3 + 3 + 5 + 5)   # dv: dO, dV; rowsum: V, dO; dk: V, dO, Q, dK; dq: dO, V, K, dQ
+    rows = 4.0 * t * 3
+    return heads * (p_reads + td + rows)
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -146,6 +173,21 @@ def make_inputs(cfg: dict, heads: range, device: torch.device, seed: int = 1234)
     return head_inputs(heads, cfg["t"], cfg["d"], dtype, device, seed=seed, scale_in=cfg["scale_in"])
 
 
+def from_p_step(x: dict, causal: bool):
+    """Forward writing P, then the first-order backward from P through the
+    reference-compatible backward_stubs helpers (the data flow of the reference's
+    save_p_triton_full backward, triton_attention.py:354-362)."""
+    from testtimeideas_b200 import _lib
+    from ttt_kernels import backward_stubs as bs
+    q, k, v, do = x["q"], x["k"], x["v"], x["do"]
+    scale = 1.0 / math.sqrt(q.shape[-1])
+    _, _, p = _lib.attn_fwd(q, k, v, causal, scale, save_p=True)
+    dv = bs.triton_attn_bwd_dv_from_p(p, do)
+    rs = bs.triton_attn_rowsum_from_p(p, do, v, causal=causal)
+    dq, dk = bs.triton_attn_bwd_dqdk_from_p(q, k, v, do, p, rs, causal=causal, scale=scale)
+    return dq, dk, dv
+
+
 def gradgrad_step(x: dict, causal: bool):
     """One step through the public, reference-compatible API."""
     from ttt_kernels import triton_attention
@@ -206,11 +248,18 @@ def verify_sharded(cfg: dict, results, total_heads: int, device: torch.device) -
     full = [gather_heads(r, total_heads) for r in results]
     if full[0] is None:
         return None
-    ref = gradgrad_step(make_inputs(cfg, range(total_heads), device), cfg["causal"])
+    ref = step_fn(cfg)(make_inputs(cfg, range(total_heads), device), cfg["causal"])
     diffs = [float((a.float() - b.float()).abs().max()) for a, b in zip(full, ref)]
     return {"heads": total_heads, "max_abs_diff": max(diffs),
             "bit_identical": all(torch.equal(a, b) for a, b in zip(full, ref)),
             "against": "rank 0 running every head alone"}
+
+
+def step_fn(cfg: dict):
+    return from_p_step if cfg.get("step") == "from_p" else gradgrad_step
+
+
+STEP_INPUTS = {"gradgrad": ("q", "k", "v", "do", "uq", "uk", "uv"), "from_p": ("q", "k", "v", "do")}
 
 
 def run_ours(args, cfg: dict) -> None:
@@ -244,10 +293,15 @@ def run_ours(args, cfg: dict) -> None:
     def max_over_ranks(x: float) -> float:
         return _max_over_ranks(x, device=device)
 
-    x = make_inputs(cfg, mine, device)
+    step = step_fn(cfg)
+    kind = cfg.get("step", "gradgrad")
+    x = {n: t for n, t in make_inputs(cfg, mine, device).items() if n in STEP_INPUTS[kind]}
     for _ in range(args.warmup):
-        gradgrad_step(x, cfg["causal"])
+        step(x, cfg["causal"])
     _lib.check_device_errors(device)
+    # Workloads that fit in L2 get an L2 flush (a 512 MiB write) between timed
+    # steps, outside the per-step events; the others are larger than L2.
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device) if cfg.get("flush") else None
 
     # ---- device-timed region: inputs resident in HBM
     clocks = ClockSampler(local)
@@ -255,18 +309,31 @@ def run_ours(args, cfg: dict) -> None:
     torch.cuda.synchronize(device)
     _lib.profile_collect()
     _lib.profile_enable(True)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        last = gradgrad_step(x, cfg["causal"])
-    stop.record()
-    torch.cuda.synchronize(device)
+    if flush is None:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            last = step(x, cfg["causal"])
+        stop.record()
+        torch.cuda.synchronize(device)
+        dev_ms = start.elapsed_time(stop)
+    else:
+        evs = []
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            last = step(x, cfg["causal"])
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize(device)
+        dev_ms = sum(a.elapsed_time(b) for a, b in evs)
     _lib.profile_enable(False)
     prof = _lib.profile_collect()
     barrier()
     clk = clocks.stop()
     _lib.check_device_errors(device)
-    ms = max_over_ranks(start.elapsed_time(stop))
+    ms = max_over_ranks(dev_ms)
     ms_per_step = ms / args.steps
     value = step_flops(cfg, total_heads) / (ms_per_step * 1e-3) / 1e12
 
@@ -286,7 +353,7 @@ def run_ours(args, cfg: dict) -> None:
     for _ in range(e2e_steps):
         for n in dev_in:
             dev_in[n].copy_(host_in[n], non_blocking=True)
-        gg = gradgrad_step(dev_in, cfg["causal"])
+        gg = step(dev_in, cfg["causal"])
         for dst, src in zip(host_out, gg):
             dst.copy_(src, non_blocking=True)
     e1.record()
@@ -301,14 +368,24 @@ def run_ours(args, cfg: dict) -> None:
     dom = max(kern, key=lambda k: kern[k][1])
     launches, dom_ms = kern[dom]
     per_launch_ms = dom_ms / launches
-    dom_flops = ALGO_UNITS[dom] * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
-    achieved = dom_flops / (per_launch_ms * 1e-3) / 1e12
-    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     traffic = load_traffic(args.config).get(dom)
-    roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": traffic,
-                "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
-                "algorithmic_flops_per_launch": dom_flops, "ms_per_launch": per_launch_ms}
+    if dom == "from_p":
+        # HBM-bound: algorithmic bytes of the from-P launches over their time
+        dom_bytes = from_p_bytes(cfg, heads) / launches * args.steps
+        achieved = dom_bytes / (per_launch_ms * 1e-3) / 1e9
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": traffic,
+                    "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                    "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": per_launch_ms}
+    else:
+        dom_flops = ALGO_UNITS[dom] * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+        achieved = dom_flops / (per_launch_ms * 1e-3) / 1e12
+        peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": traffic,
+                    "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+                    "algorithmic_flops_per_launch": dom_flops, "ms_per_launch": per_launch_ms}
 
     gpu_launches = sum(v[0] for v in prof.values())
     kernel_ms = {k: v[1] / args.steps for k, v in kern.items()}
@@ -333,8 +410,10 @@ def run_ours(args, cfg: dict) -> None:
             "config": {"workload": cfg["workload"], "b": cfg["b"], "h": cfg["h"], "t": cfg["t"], "d": cfg["d"],
                        "causal": cfg["causal"], "global_heads": total_heads, "heads_per_gpu": heads,
                        "parallelism": f"bh-shard x{world}",
-                       "l2": "inputs larger than L2 (7 tensors of %.2f GiB per GPU)" % (
-                           x["q"].numel() * x["q"].element_size() / 2 ** 30)},
+                       "l2": ("L2 flushed (512 MiB write) between timed steps" if flush is not None else
+                              "inputs larger than L2 (%d tensors of %.2f GiB per GPU%s)" % (
+                                  len(x), x["q"].numel() * x["q"].element_size() / 2 ** 30,
+                                  ", plus P" if kind == "from_p" else ""))},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms, "steps": e2e_steps,
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
             "roofline": roofline,
