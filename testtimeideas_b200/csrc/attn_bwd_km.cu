@@ -17,16 +17,20 @@
 // producer. The per-query statistics (lse2, delta, gamma, rho) of each tile
 // arrive with it through TMA and are read with broadcast 16-byte loads.
 //
-// Where the elementwise results live (ETM = "E in TMEM"):
-//   shared memory (kBwdKV, d=128): swizzled K-major tiles, SS products;
-//   a dedicated TMEM region (kBwdKV d=64, kBwd2KV d=64): packed 16-bit pairs,
-//     A-from-TMEM products, no ordering constraint;
-//   TMEM columns shared with the first score tiles (kBwd2KV d=128, where four
-//     64-wide score tiles and two 128-wide accumulators fill all 512 columns):
-//     each tile first issues the score products that do not touch those
-//     columns (dP^T, (dO u_v^T)^T), then the previous tile's accumulate
-//     products, waits for them to finish reading, and only then issues the
-//     products that overwrite the shared columns (K [Q; u_q]^T, u_k Q^T).
+// The elementwise results E (16-bit P^T, dS^T | dS^T, G_S^T, G_dP^T) live in
+// TMEM as packed pairs and are the A operand of the accumulate products:
+//   kBwdKV: over the S^T columns of the tile's own score buffer (two
+//     buffers), each thread writing only the columns it read (its half's 32
+//     S^T columns take its 16 P^T and 16 dS^T words);
+//   kBwd2KV d=64: a dedicated region;
+//   kBwd2KV d=128, where four 64-wide score tiles and two 128-wide
+//     accumulators fill all 512 columns: columns shared with the first score
+//     tiles. Each tile first issues the score products that do not touch them
+//     (dP^T, (dO u_v^T)^T), then the previous tile's accumulate products, then
+//     the products that overwrite the shared columns (K [Q; u_q]^T, u_k Q^T).
+// Reusing E's columns for the next score product needs no wait: tcgen05.mma
+// ops issued by one thread execute in issue order, so the accumulate product
+// has read E before a later product writes there.
 //
 // In the double backward the streamed Q and u_q tiles are stacked in one
 // panel so that K [Q; u_q]^T produces [S^T | K u_q^T] as a single N=128
@@ -59,10 +63,10 @@ struct KmCfg {
   static constexpr int STAT_BYTES = BM * 4;
   static constexpr int STAGE_TX = ST0_BYTES + ST1_BYTES + NSTAT * STAT_BYTES;  // bytes TMA delivers per stage
   static constexpr int STAGE = (STAGE_TX + 1023) / 1024 * 1024;               // pitch keeps tiles 1024-aligned
-  static constexpr int TILE_E = BK * BM * 2;
   static constexpr int E_COLS = BM / 2;  // TMEM columns of one packed 16-bit E tile
   // TMEM layout
-  static constexpr bool ETM = BWD2 || D == 64;
+  static constexpr bool E_OWN = !BWD2;  // E over the S^T columns of its own score buffer
+  static constexpr bool ETM = BWD2;     // E in a region of its own (dedicated or shared)
   static constexpr int NBUF_WANT = (2 * NSC * BM + NA * D + (ETM ? NE * E_COLS : 0) <= 512) ? 2 : 1;
   static constexpr int NBUF = NBUF_WANT;
   static constexpr int SC_COLS = NBUF * NSC * BM;
@@ -74,13 +78,11 @@ struct KmCfg {
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
   static_assert(!E_OVERLAP || NBUF == 1, "overlapping E needs a single score buffer");
-  static constexpr int E_SMEM = ETM ? 0 : NE * TILE_E;
   static constexpr int BAR_BYTES = 20 * 8;
-  static constexpr int FIXED = NR * TILE_R + E_SMEM + BAR_BYTES + (STAGE_TX - STAGE);
+  static constexpr int FIXED = NR * TILE_R + BAR_BYTES + (STAGE_TX - STAGE);
   static constexpr int NSTAGE = (FIXED + 4 * STAGE + 1024 <= 232448) ? 4 : (FIXED + 3 * STAGE + 1024 <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
-  static constexpr int OFF_E = OFF_R + NR * TILE_R;
-  static constexpr int OFF_S = OFF_E + E_SMEM;
+  static constexpr int OFF_S = OFF_R + NR * TILE_R;
   static constexpr int OFF_BAR = OFF_S + (NSTAGE - 1) * STAGE + STAGE_TX;  // the last stage needs no padding
   static constexpr int BODY = OFF_BAR + BAR_BYTES;
   // Reserve room to realign the dynamic shared-memory base to 1024 bytes when
@@ -115,7 +117,6 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   }
   uint8_t* sR = smem + C::OFF_R;
   uint8_t* sS = smem + C::OFF_S;
-  uint8_t* sE = smem + C::OFF_E;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
   uint64_t* l_full = bars + 1;    // [4]
@@ -135,7 +136,6 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   auto statS = [&](int s, int t) {
     return reinterpret_cast<const float*>(sS + s * C::STAGE + C::ST0_BYTES + C::ST1_BYTES + t * C::STAT_BYTES);
   };
-  auto tileE = [&](int t) { return sE + t * C::TILE_E; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -170,6 +170,16 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const uint32_t tAcc1 = tAcc0 + D;          // dV / dd_V
   const uint32_t tE = tmem + C::E_COL;       // packed E tiles (ETM)
   Guard g{abort_flag, p.err};
+  // TMEM column of K-step kk (16 queries) of E tile j of tile n. Outside a
+  // dedicated region each half of the elementwise warps (queries 32h..32h+31)
+  // writes E only over score columns it has read itself: the first score tile's
+  // 32 columns take E tiles 0 and 1 (16 words each), the second's take tile 2.
+  auto e_col = [&](int j, int kk, int n) -> uint32_t {
+    if constexpr (C::E_DEDICATED) return tE + j * C::E_COLS + kk * 8;
+    const uint32_t off = 32 * (kk >> 1) + (kk & 1) * 8 + (j == 2 ? BM : 16 * j);
+    if constexpr (C::E_OWN) return tmem + (n % NBUF) * C::NSC * BM + off;
+    return tmem + off;
+  };
 
   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
@@ -248,13 +258,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
 #pragma unroll
           for (int kk = 0; kk < BM / 16; ++kk) {
             const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
-            if constexpr (C::ETM) {
-              umma_ts(tAcc1, tE + 0 * C::E_COLS + kk * 8, desc_mnmajor(bDO, BM, kk), id_acc, a);
-              umma_ts(tAcc0, tE + 1 * C::E_COLS + kk * 8, desc_mnmajor(bQ, SR0, kk), id_acc, a);
-            } else {
-              umma_ss(tAcc1, desc_kmajor(smem_u32(tileE(0)), BK, kk), desc_mnmajor(bDO, BM, kk), id_acc, a);
-              umma_ss(tAcc0, desc_kmajor(smem_u32(tileE(1)), BK, kk), desc_mnmajor(bQ, SR0, kk), id_acc, a);
-            }
+            umma_ts(tAcc1, e_col(0, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, a);
+            umma_ts(tAcc0, e_col(1, kk, n), desc_mnmajor(bQ, SR0, kk), id_acc, a);
           }
         } else {
           // dd_K += dS^T u_q + G_S^T Q ; dd_V += G_dP^T dO   (E in TMEM)
@@ -262,9 +267,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
 #pragma unroll
           for (int kk = 0; kk < BM / 16; ++kk) {
             const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
-            umma_ts(tAcc0, tE + 0 * C::E_COLS + kk * 8, desc_mnmajor(bUQ, SR0, kk), id_acc, a);
-            umma_ts(tAcc0, tE + 1 * C::E_COLS + kk * 8, desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
-            umma_ts(tAcc1, tE + 2 * C::E_COLS + kk * 8, desc_mnmajor(bDO, BM, kk), id_acc, a);
+            umma_ts(tAcc0, e_col(0, kk, n), desc_mnmajor(bUQ, SR0, kk), id_acc, a);
+            umma_ts(tAcc0, e_col(1, kk, n), desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
+            umma_ts(tAcc1, e_col(2, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, a);
           }
         }
       };
@@ -290,15 +295,12 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           if (!(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
           tc_fence_after();
           acc_products(n - 1);
-          umma_commit(e_empty);
+          if constexpr (C::E_DEDICATED) umma_commit(e_empty);
           umma_commit(l_empty + (n - 1) % NSTAGE);
-          if constexpr (C::E_OVERLAP) umma_commit(e_done);
         }
         if constexpr (C::E_OVERLAP) {
           if (has_scores) {
-            // E(n-1) must be fully read before S^T / G_dS^T of tile n overwrite its columns.
-            if (n >= 1 && !(ok = mbar_wait(e_done, (n - 1) & 1, g, 5))) break;
-            tc_fence_after();
+            // overwrites the columns of E(n-1), which the products just issued read first
             scores_e_cols(base, s);
             umma_commit(s_full + sb);
           }
@@ -389,28 +391,32 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           }
         }
       }
-      if (n >= 1 && !mbar_wait(e_empty, (n - 1) & 1, g, 7)) { ok = false; break; }
-      if constexpr (C::ETM) {
-        // packed 16-bit pairs: this thread's 32 columns -> 16 TMEM columns per E tile
-        const uint32_t eb = tE + lane_off + (c0 >> 1);
+      // A dedicated E region is reused every tile: wait until the previous tile's
+      // accumulate products have read it. E over score columns needs no wait: the
+      // products that overwrite those columns are issued after this tile's e_full.
+      if (C::E_DEDICATED && n >= 1 && !mbar_wait(e_empty, (n - 1) & 1, g, 7)) { ok = false; break; }
+      {
+        // this thread's 16 words of E tile j (see e_col)
+        auto e_put = [&](int j) -> uint32_t {
+          if constexpr (C::E_DEDICATED) return tE + lane_off + (c0 >> 1) + j * C::E_COLS;
+          const uint32_t off = 32 * half + (j == 2 ? BM : 16 * j);
+          if constexpr (C::E_OWN) return tmem + lane_off + sb * C::NSC * BM + off;
+          return tmem + lane_off + off;
+        };
         uint32_t w[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(sv[2 * j], sv[2 * j + 1]);
-        tmem_st16_raw(eb + 0 * C::E_COLS, w);
+        tmem_st16_raw(e_put(0), w);
 #pragma unroll
         for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(dp[2 * j], dp[2 * j + 1]);
-        tmem_st16_raw(eb + 1 * C::E_COLS, w);
+        tmem_st16_raw(e_put(1), w);
         if constexpr (C::BWD2) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(gd[2 * j], gd[2 * j + 1]);
-          tmem_st16_raw(eb + 2 * C::E_COLS, w);
+          tmem_st16_raw(e_put(2), w);
         }
         tmem_wait_st();
         tc_fence_before();
-      } else {
-        store_cols<BF16, CPW>(tileE(0), BK, r, c0, sv);
-        store_cols<BF16, CPW>(tileE(1), BK, r, c0, dp);
-        fence_async_smem();
       }
       mbar_arrive(e_full);
     }
