@@ -200,13 +200,15 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       constexpr uint32_t id_acc = idesc_f16(128, D, BF16, false, true);
       const uint32_t aQ = smem_u32(tileR(0)), aDO = smem_u32(tileR(1));
       const uint32_t aUQ = C::BWD2 ? smem_u32(tileR(2)) : 0u;
-      auto issue_scores = [&](int n) -> bool {
+      using LS = KOff2<KOffK<BM>, KOffK<SR>>;  // score products: both operands K-major
+      using LA = KOff2<KOffK<BM>, KOffMN>;     // accumulate products: E K-major, streamed tile MN-major
+      // Score products of tile n; the last product's batch probes (bar0, par0) and (bar1, par1).
+      auto issue_scores = [&](int n, const uint64_t* bar0, uint32_t par0, const uint64_t* bar1,
+                              uint32_t par1) -> uint32_t {
         const int sb = n % NBUF, s = n % NSTAGE;
-        if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2)) return false;
-        if (n >= NBUF && !mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3)) return false;
-        tc_fence_after();
         const uint32_t base = tmem + sb * C::NSC * BN;
         const uint32_t b0 = smem_u32(tileS(s, 0)), b1 = smem_u32(tileS(s, 1));
+        uint32_t seen;
         if constexpr (C::BWD2) {
           // [S | Q u_k^T] = Q [K; u_k]^T ; G_dS/scale += u_q K^T ; [dP | dO u_v^T] = dO [V; u_v]^T
           if constexpr (C::RT_Q) {
@@ -224,71 +226,99 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
             for (int kk = 0; kk < D / 16; ++kk)
               umma_ss(base + C::C_GDS, desc_kmajor(aUQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, 1u);
           }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n2, kk > 0);
+          seen = issue_ss<D / 16, LS>(base + C::C_DP, desc_kmajor(aDO, BM, 0), desc_kmajor(b1, SR, 0), id_n2, 0u,
+                                      bar0, par0, bar1, par1);
         } else if constexpr (C::RT_Q && C::RT_DO) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ts(base + C::C_S, tQ + kk * 8, desc_kmajor(b0, SR, kk), id_n1, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ts(base + C::C_DP, tDO + kk * 8, desc_kmajor(b1, SR, kk), id_n1, kk > 0);
+          seen = issue_ts<D / 16, LS>(base + C::C_DP, tDO, desc_kmajor(b1, SR, 0), id_n1, 0u, bar0, par0, bar1, par1);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_S, desc_kmajor(aQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_DP, desc_kmajor(aDO, BM, kk), desc_kmajor(b1, SR, kk), id_n1, kk > 0);
+          seen = issue_ss<D / 16, LS>(base + C::C_DP, desc_kmajor(aDO, BM, 0), desc_kmajor(b1, SR, 0), id_n1, 0u,
+                                      bar0, par0, bar1, par1);
         }
         umma_commit(s_full + sb);
         if constexpr (C::NA == 0) umma_commit(l_empty + s);
-        return true;
+        return seen;
       };
-      auto issue_acc = [&](int n) -> bool {
+      // Accumulate products of tile n (its e_full already seen); probes as above.
+      auto issue_acc = [&](int n, const uint64_t* bar0, uint32_t par0, const uint64_t* bar1,
+                           uint32_t par1) -> uint32_t {
         const int s = n % NSTAGE;
-        if (!mbar_wait(e_full, n & 1, g, 4)) return false;
-        tc_fence_after();
         const uint32_t bK = smem_u32(tileS(s, 0)), bV = smem_u32(tileS(s, 1));
         const uint32_t e0 = smem_u32(tileE(s, 0));
+        const uint32_t fresh = n > 0 ? 1u : 0u;
+        uint32_t seen = 0;
         if constexpr (KIND == kBwdQ) {
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bK, SR, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+          seen = issue_ss<BN / 16, LA>(tAcc0, desc_kmajor(e0, BM, 0), desc_mnmajor(bK, SR, 0), id_acc, fresh, bar0,
+                                       par0, bar1, par1);
         } else {
           const uint32_t bUK = bK + BN * 128, bUV = bV + BN * 128;
           const uint32_t e1 = smem_u32(tileE(s, 1));
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
             umma_ss(tAcc0, desc_kmajor(e0, BM, kk), desc_mnmajor(bUK, SR, kk), id_acc, (n > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (!GDO) {
+            seen = issue_ss<BN / 16, LA>(tAcc0, desc_kmajor(e1, BM, 0), desc_mnmajor(bK, SR, 0), id_acc, 1u, bar0,
+                                         par0, bar1, par1);
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ss(tAcc0, desc_kmajor(e1, BM, kk), desc_mnmajor(bK, SR, kk), id_acc, 1u);
-          if constexpr (GDO) {
+            for (int kk = 0; kk < BN / 16; ++kk)
+              umma_ss(tAcc0, desc_kmajor(e1, BM, kk), desc_mnmajor(bK, SR, kk), id_acc, 1u);
             const uint32_t e2 = smem_u32(tileE(s, 2)), e3 = smem_u32(tileE(s, 3));
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk)
               umma_ss(tAcc1, desc_kmajor(e2, BM, kk), desc_mnmajor(bV, SR, kk), id_acc,
                       (n > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk)
-              umma_ss(tAcc1, desc_kmajor(e3, BM, kk), desc_mnmajor(bUV, SR, kk), id_acc, 1u);
+            seen = issue_ss<BN / 16, LA>(tAcc1, desc_kmajor(e3, BM, 0), desc_mnmajor(bUV, SR, 0), id_acc, 1u, bar0,
+                                         par0, bar1, par1);
           }
         }
         if constexpr (!C::EIS) umma_commit(e_empty);
         umma_commit(l_empty + s);
-        return true;
+        return seen;
       };
       bool ok = mbar_wait(res_full, 0, g, 1);
+      // res_full's phase 0 completed above: a probe of it always succeeds (an unused probe slot)
+      const uint64_t* done = res_full;
+      bool have_l = false, have_s = false;  // the next score step's barriers already seen complete
       for (int n = 0; ok && n < n_tiles; ++n) {
-        ok = issue_scores(n);
-        if constexpr (C::NA > 0) {
-          if (ok && n >= 1) ok = issue_acc(n - 1);
+        const int sb = n % NBUF, s = n % NSTAGE;
+        if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+        if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+        tc_fence_after();
+        // barriers of tile n+1's score step
+        const bool nxt = n + 1 < n_tiles;
+        const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
+        const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
+        const bool need_s = nxt && n + 1 >= NBUF;
+        const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
+        const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
+        if (C::NA > 0 && n >= 1) {
+          // tile n-1's accumulate step follows: probe its e_full while issuing these scores
+          const uint32_t seen = issue_scores(n, e_full, (n - 1) & 1, bl, pl);
+          if (!(seen & 1) && !(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
+          tc_fence_after();
+          const uint32_t seen2 = issue_acc(n - 1, bl, pl, bs, ps);
+          have_l = ((seen >> 1) & 1) || (seen2 & 1);
+          have_s = (seen2 >> 1) & 1;
+        } else {
+          const uint32_t seen = issue_scores(n, bl, pl, bs, ps);
+          have_l = seen & 1;
+          have_s = (seen >> 1) & 1;
         }
       }
       if constexpr (C::NA > 0) {
-        if (ok) ok = issue_acc(n_tiles - 1);
+        if (ok && n_tiles > 0) {
+          ok = mbar_wait(e_full, (n_tiles - 1) & 1, g, 4);
+          if (ok) {
+            tc_fence_after();
+            issue_acc(n_tiles - 1, done, 0u, done, 0u);
+          }
+        }
         if (ok) umma_commit(acc_full);
       }
       umma_commit(drain);

@@ -273,6 +273,124 @@ TTT_DEV uint64_t desc_mnmajor(uint32_t tile_saddr, int rows, int kk) {
   return sdesc_sw128(a, static_cast<uint32_t>(rows * 128), 1024);
 }
 
+// ---------------------------------------------------------------- batched issue with barrier probes
+// A satisfied mbarrier.try_wait takes ~160 cycles on the issuing thread, and the
+// tensor core's instruction queue covers only ~40 cycles of issue gaps, so
+// every wait between UMMA batches idles the tensor pipe. These helpers issue
+// the K-steps of one product (4 or 8 UMMAs, kind::f16) in a single asm
+// statement that starts with try_wait probes of two barrier phases and reads
+// their results only after the UMMAs are queued: the probes' latency overlaps
+// the issue. The returned bits (bit0: bar0's phase par0 complete, bit1: bar1's)
+// let the caller skip waits that are already satisfied; a clear bit means
+// "not yet", and the caller falls back to a bounded mbar_wait.
+//
+// L describes the per-K-step descriptor offsets (in 16-byte units) of the A and
+// B operands relative to K-step 0: L::a(kk), L::b(kk), compile-time constants.
+template <int ROWS>
+struct KOffK {  // K-major PL tile with ROWS rows: K-step kk at panel kk/4, byte (kk%4)*32
+  static constexpr int at(int kk) { return ((kk >> 2) * ROWS * 128 + (kk & 3) * 32) >> 4; }
+};
+struct KOffMN {  // MN-major PL tile: K-step kk at row 16*kk
+  static constexpr int at(int kk) { return (kk * 2048) >> 4; }
+};
+template <class A, class B>
+struct KOff2 {
+  static constexpr int a(int kk) { return A::at(kk); }
+  static constexpr int b(int kk) { return B::at(kk); }
+};
+
+template <class L>
+TTT_DEV uint32_t umma_ss4_probe(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
+                                 const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b64 da, db;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], %7, %8, %10, q;\n\t"
+      "add.s64 da, %7, %11; add.s64 db, %8, %14; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %12; add.s64 db, %8, %15; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %13; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "l"(a0), "l"(b0), "r"(acc_first),
+        "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
+template <class L>
+TTT_DEV uint32_t umma_ts4_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
+                                 const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %10, q;\n\t"
+      "add.u32 ta, %7, 8; add.s64 db, %8, %11; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 16; add.s64 db, %8, %12; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 24; add.s64 db, %8, %13; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(acc_first),
+        "r"(idesc), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
+template <class L>
+TTT_DEV uint32_t umma_ss8_probe(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
+                                 const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b64 da, db;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], %7, %8, %10, q;\n\t"
+      "add.s64 da, %7, %11; add.s64 db, %8, %18; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %12; add.s64 db, %8, %19; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %13; add.s64 db, %8, %20; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %14; add.s64 db, %8, %21; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %15; add.s64 db, %8, %22; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %16; add.s64 db, %8, %23; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "add.s64 da, %7, %17; add.s64 db, %8, %24; tcgen05.mma.cta_group::1.kind::f16 [%6], da, db, %10, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "l"(a0), "l"(b0), "r"(acc_first),
+        "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::a(4)), "n"(L::a(5)), "n"(L::a(6)), "n"(L::a(7)), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3)), "n"(L::b(4)), "n"(L::b(5)), "n"(L::b(6)), "n"(L::b(7))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
+template <class L>
+TTT_DEV uint32_t umma_ts8_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
+                                 const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %10, q;\n\t"
+      "add.u32 ta, %7, 8; add.s64 db, %8, %11; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 16; add.s64 db, %8, %12; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 24; add.s64 db, %8, %13; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 32; add.s64 db, %8, %14; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 40; add.s64 db, %8, %15; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 48; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, 56; add.s64 db, %8, %17; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(acc_first),
+        "r"(idesc), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3)), "n"(L::b(4)), "n"(L::b(5)), "n"(L::b(6)), "n"(L::b(7))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
 // Byte offset of element (r, c) in PL(R, C) (16-bit elements).
 TTT_DEV uint32_t pl_offset(int R, int r, int c) {
   const int panel = c >> 6;
