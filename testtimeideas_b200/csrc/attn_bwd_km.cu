@@ -36,10 +36,18 @@
 // panel so that K [Q; u_q]^T produces [S^T | K u_q^T] as a single N=128
 // product (an M=128 UMMA with N <= 64 costs about as much as one with N=128).
 // Causal: query tiles that end before the CTA's first key are skipped.
+#include <type_traits>
+
 #include "attn_pipe.cuh"
 #include "kernels.h"
 
 namespace ttt {
+
+// Columns of K-step kk of an E tile written over score columns: queries
+// 32h..32h+31 (half h of the elementwise warps) hold K-steps 2h and 2h+1.
+struct KOffEHalf {
+  static constexpr int at(int kk) { return 32 * (kk >> 1) + (kk & 1) * 8; }
+};
 
 template <int D, int KIND>
 struct KmCfg {
@@ -220,49 +228,59 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       constexpr uint32_t id_acc = idesc_f16(128, D, BF16, false, true);
       const uint32_t aK = smem_u32(tileR(0)), aV = smem_u32(tileR(1));
       const uint32_t aUK = C::BWD2 ? smem_u32(tileR(2)) : 0u, aUV = C::BWD2 ? smem_u32(tileR(3)) : 0u;
+      using LD = KOff2<KOffK<BK>, KOffK<BM>>;   // resident A, streamed dO (rows BM)
+      using LQ = KOff2<KOffK<BK>, KOffK<SR0>>;  // resident A, streamed [Q; u_q] (rows SR0)
+      using LE = KOff2<std::conditional_t<C::E_DEDICATED, KOffT, KOffEHalf>, KOffMN>;  // E from TMEM, MN-major B
+      // Probes pay off only with two score buffers: with one, each tile first waits for
+      // the compute warps to read the previous scores, a wait no probe can skip.
+      constexpr bool PR = NBUF == 2;
       // Score products whose output columns never hold E: dP^T (and (dO u_v^T)^T).
-      auto scores_free_cols = [&](uint32_t base, int s) {
+      // Each group issues its last product as one batch with two barrier probes.
+      auto scores_free_cols = [&](uint32_t base, int s, const uint64_t* b0_, uint32_t p0_, const uint64_t* b1_,
+                                  uint32_t p1_) -> uint32_t {
         const uint32_t b1 = smem_u32(st1(s));
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(base + C::C_DP, desc_kmajor(aV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
         if constexpr (C::BWD2) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_UV, desc_kmajor(aUV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
+            umma_ss(base + C::C_DP, desc_kmajor(aV, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
+          return issue_ss<D / 16, LD, PR>(base + C::C_UV, desc_kmajor(aUV, BK, 0), desc_kmajor(b1, BM, 0), id_n1, 0u, b0_,
+                                      p0_, b1_, p1_);
+        } else {
+          return issue_ss<D / 16, LD, PR>(base + C::C_DP, desc_kmajor(aV, BK, 0), desc_kmajor(b1, BM, 0), id_n1, 0u, b0_,
+                                      p0_, b1_, p1_);
         }
       };
       // Score products into columns that E may share: S^T (and G_dS^T).
-      auto scores_e_cols = [&](uint32_t base, int s) {
+      auto scores_e_cols = [&](uint32_t base, int s, const uint64_t* b0_, uint32_t p0_, const uint64_t* b1_,
+                               uint32_t p1_) -> uint32_t {
         const uint32_t b0 = smem_u32(st0(s));
         if constexpr (C::BWD2) {
           // [S^T | K u_q^T] = K [Q; u_q]^T ; G_dS^T/scale += u_k Q^T
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(base + C::C_S, desc_kmajor(aK, BK, kk), desc_kmajor(b0, SR0, kk), id_n2, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_GDS, desc_kmajor(aUK, BK, kk), desc_kmajor(b0, SR0, kk), id_n1, 1u);
+          return issue_ss<D / 16, LQ, PR>(base + C::C_GDS, desc_kmajor(aUK, BK, 0), desc_kmajor(b0, SR0, 0), id_n1, 1u,
+                                      b0_, p0_, b1_, p1_);
         } else {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(base + C::C_S, desc_kmajor(aK, BK, kk), desc_kmajor(b0, SR0, kk), id_n1, kk > 0);
+          return issue_ss<D / 16, LQ, PR>(base + C::C_S, desc_kmajor(aK, BK, 0), desc_kmajor(b0, SR0, 0), id_n1, 0u, b0_,
+                                      p0_, b1_, p1_);
         }
       };
-      auto acc_products = [&](int n) {
+      auto acc_products = [&](int n, const uint64_t* b0_, uint32_t p0_, const uint64_t* b1_, uint32_t p1_) -> uint32_t {
         const int s = n % NSTAGE;
         const uint32_t bQ = smem_u32(st0(s)), bDO = smem_u32(st1(s));
         const uint32_t acc_first = n > 0 ? 1u : 0u;
         if constexpr (!C::BWD2) {
           // dV += P^T dO ; dK += dS^T Q
 #pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk) {
-            const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
-            umma_ts(tAcc1, e_col(0, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, a);
-            umma_ts(tAcc0, e_col(1, kk, n), desc_mnmajor(bQ, SR0, kk), id_acc, a);
-          }
+          for (int kk = 0; kk < BM / 16; ++kk)
+            umma_ts(tAcc1, e_col(0, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, (acc_first || kk > 0) ? 1u : 0u);
+          return issue_ts<BM / 16, LE, PR>(tAcc0, e_col(1, 0, n), desc_mnmajor(bQ, SR0, 0), id_acc, acc_first, b0_, p0_,
+                                       b1_, p1_);
         } else {
-          // dd_K += dS^T u_q + G_S^T Q ; dd_V += G_dP^T dO   (E in TMEM)
+          // dd_K += dS^T u_q + G_S^T Q ; dd_V += G_dP^T dO   (E in TMEM). The three products
+          // alternate per K-step (faster than grouping them), so this step carries no probes.
+          (void)b0_, (void)p0_, (void)b1_, (void)p1_;
           const uint32_t bUQ = bQ + BM * 128;
 #pragma unroll
           for (int kk = 0; kk < BM / 16; ++kk) {
@@ -271,40 +289,59 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             umma_ts(tAcc0, e_col(1, kk, n), desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
             umma_ts(tAcc1, e_col(2, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, a);
           }
+          return 0u;
         }
       };
       bool ok = mbar_wait(res_full, 0, g, 1);
+      // res_full's phase 0 completed above: a probe of it always succeeds (an unused probe slot)
+      const uint64_t* done = res_full;
+      bool have_l = false, have_s = false;  // this tile's l_full / s_free already seen complete by a probe
       for (int n = 0; ok && n <= n_tiles; ++n) {
         const bool has_scores = n < n_tiles;
         const int sb = n % NBUF, s = n % NSTAGE;
         const uint32_t base = tmem + sb * C::NSC * BM;
+        // barriers of tile n+1's score products, probed while this iteration issues
+        const bool nxt = n + 1 < n_tiles;
+        const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
+        const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
+        const bool need_s = nxt && n + 1 >= NBUF;
+        const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
+        const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
+        const uint64_t* be = n >= 1 ? e_full : done;
+        const uint32_t pe = n >= 1 ? (n - 1) & 1 : 0u;
+        bool next_l = false, next_s = false, seen_e = false;
         if (has_scores) {
-          if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
-          if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+          if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+          if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
           tc_fence_after();
-          if constexpr (C::E_OVERLAP) {
-            scores_free_cols(base, s);
-          } else {
-            scores_e_cols(base, s);
-            scores_free_cols(base, s);
-            umma_commit(s_full + sb);
-          }
+          if constexpr (!C::E_OVERLAP) scores_e_cols(base, s, done, 0u, done, 0u);
+          const uint32_t seen = scores_free_cols(base, s, be, pe, bl, pl);
+          if constexpr (!C::E_OVERLAP) umma_commit(s_full + sb);
+          seen_e = seen & 1;
+          next_l = (seen >> 1) & 1;
         }
         if (n >= 1) {
           // accumulate products of tile n-1
-          if (!(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
+          if (!seen_e && !(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
           tc_fence_after();
-          acc_products(n - 1);
+          const uint32_t seen = acc_products(n - 1, bl, pl, bs, ps);
           if constexpr (C::E_DEDICATED) umma_commit(e_empty);
           umma_commit(l_empty + (n - 1) % NSTAGE);
+          next_l = next_l || (seen & 1);
+          next_s = (seen >> 1) & 1;
         }
         if constexpr (C::E_OVERLAP) {
           if (has_scores) {
             // overwrites the columns of E(n-1), which the products just issued read first
-            scores_e_cols(base, s);
+            // (tile n+1 also needs s_free(n), which cannot be complete before these scores are)
+            const uint32_t seen = scores_e_cols(base, s, bl, pl, done, 0u);
             umma_commit(s_full + sb);
+            next_l = next_l || (seen & 1);
+            next_s = next_s || ((seen >> 1) & 1);
           }
         }
+        have_l = next_l;
+        have_s = next_s;
       }
       if (ok) umma_commit(acc_full);
       umma_commit(drain);

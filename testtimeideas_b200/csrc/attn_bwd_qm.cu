@@ -232,7 +232,8 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ts(base + C::C_S, tQ + kk * 8, desc_kmajor(b0, SR, kk), id_n1, kk > 0);
-          seen = issue_ts<D / 16, LS>(base + C::C_DP, tDO, desc_kmajor(b1, SR, 0), id_n1, 0u, bar0, par0, bar1, par1);
+          seen = issue_ts<D / 16, KOff2<KOffT, KOffK<SR>>>(base + C::C_DP, tDO, desc_kmajor(b1, SR, 0), id_n1, 0u, bar0,
+                                                          par0, bar1, par1);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)

@@ -111,14 +111,16 @@ TTT_DEV F2 fma2(F2 a, F2 b, F2 c) {
 }
 
 // The K-steps of one product, issued as one batch that also probes two barrier
-// phases (see umma_ss8_probe). K-step counts without a probe helper issue
-// plainly and report nothing as seen (0).
-template <int KS, class L>
+// phases (see umma_ss8_probe). With PROBE false, or a K-step count without a
+// probe helper, the K-steps are issued plainly and nothing is reported as seen
+// (0): a probe costs ~44 cycles of issue, a loss where the waits it could
+// replace are rarely satisfied in time.
+template <int KS, class L, bool PROBE = true>
 TTT_DEV uint32_t issue_ss(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
                           const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
-  if constexpr (KS == 8) {
+  if constexpr (PROBE && KS == 8) {
     return umma_ss8_probe<L>(d, a0, b0, idesc, acc_first, bar0, par0, bar1, par1);
-  } else if constexpr (KS == 4) {
+  } else if constexpr (PROBE && KS == 4) {
     return umma_ss4_probe<L>(d, a0, b0, idesc, acc_first, bar0, par0, bar1, par1);
   } else {
 #pragma unroll
@@ -127,16 +129,16 @@ TTT_DEV uint32_t issue_ss(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, 
     return 0u;
   }
 }
-template <int KS, class L>
+template <int KS, class L, bool PROBE = true>
 TTT_DEV uint32_t issue_ts(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
                           const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
-  if constexpr (KS == 8) {
+  if constexpr (PROBE && KS == 8) {
     return umma_ts8_probe<L>(d, a0, b0, idesc, acc_first, bar0, par0, bar1, par1);
-  } else if constexpr (KS == 4) {
+  } else if constexpr (PROBE && KS == 4) {
     return umma_ts4_probe<L>(d, a0, b0, idesc, acc_first, bar0, par0, bar1, par1);
   } else {
 #pragma unroll
-    for (int kk = 0; kk < KS; ++kk) umma_ts(d, a0 + kk * 8, b0 + L::b(kk), idesc, kk > 0 ? 1u : acc_first);
+    for (int kk = 0; kk < KS; ++kk) umma_ts(d, a0 + L::a(kk), b0 + L::b(kk), idesc, kk > 0 ? 1u : acc_first);
     return 0u;
   }
 }

@@ -284,14 +284,18 @@ TTT_DEV uint64_t desc_mnmajor(uint32_t tile_saddr, int rows, int kk) {
 // let the caller skip waits that are already satisfied; a clear bit means
 // "not yet", and the caller falls back to a bounded mbar_wait.
 //
-// L describes the per-K-step descriptor offsets (in 16-byte units) of the A and
-// B operands relative to K-step 0: L::a(kk), L::b(kk), compile-time constants.
+// L describes the per-K-step offsets of the A and B operands relative to
+// K-step 0, as compile-time constants L::a(kk), L::b(kk): descriptor units (16
+// bytes) for shared-memory operands, columns for an A operand in TMEM.
 template <int ROWS>
 struct KOffK {  // K-major PL tile with ROWS rows: K-step kk at panel kk/4, byte (kk%4)*32
   static constexpr int at(int kk) { return ((kk >> 2) * ROWS * 128 + (kk & 3) * 32) >> 4; }
 };
 struct KOffMN {  // MN-major PL tile: K-step kk at row 16*kk
   static constexpr int at(int kk) { return (kk * 2048) >> 4; }
+};
+struct KOffT {  // A operand in TMEM, K-steps packed contiguously: 8 columns per K-step
+  static constexpr int at(int kk) { return kk * 8; }
 };
 template <class A, class B>
 struct KOff2 {
@@ -330,13 +334,13 @@ TTT_DEV uint32_t umma_ts4_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t i
       "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
       "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %10, q;\n\t"
-      "add.u32 ta, %7, 8; add.s64 db, %8, %11; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 16; add.s64 db, %8, %12; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 24; add.s64 db, %8, %13; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %11; add.s64 db, %8, %14; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %12; add.s64 db, %8, %15; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %13; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
       "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
       : "=r"(r0), "=r"(r1)
       : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(acc_first),
-        "r"(idesc), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3))
+        "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3))
       : "memory");
   return r0 | (r1 << 1);
 }
@@ -376,17 +380,17 @@ TTT_DEV uint32_t umma_ts8_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t i
       "mbarrier.try_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
       "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %10, q;\n\t"
-      "add.u32 ta, %7, 8; add.s64 db, %8, %11; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 16; add.s64 db, %8, %12; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 24; add.s64 db, %8, %13; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 32; add.s64 db, %8, %14; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 40; add.s64 db, %8, %15; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 48; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
-      "add.u32 ta, %7, 56; add.s64 db, %8, %17; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %11; add.s64 db, %8, %18; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %12; add.s64 db, %8, %19; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %13; add.s64 db, %8, %20; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %14; add.s64 db, %8, %21; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %15; add.s64 db, %8, %22; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %16; add.s64 db, %8, %23; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %17; add.s64 db, %8, %24; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
       "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
       : "=r"(r0), "=r"(r1)
       : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(acc_first),
-        "r"(idesc), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3)), "n"(L::b(4)), "n"(L::b(5)), "n"(L::b(6)), "n"(L::b(7))
+        "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::a(4)), "n"(L::a(5)), "n"(L::a(6)), "n"(L::a(7)), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3)), "n"(L::b(4)), "n"(L::b(5)), "n"(L::b(6)), "n"(L::b(7))
       : "memory");
   return r0 | (r1 << 1);
 }
