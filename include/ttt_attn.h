@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define TTT_ATTN_ABI_VERSION 1
+#define TTT_ATTN_ABI_VERSION 2
 
 enum ttt_status {
   TTT_OK = 0,
@@ -65,6 +65,14 @@ typedef struct {
   int32_t dtype;  /* enum ttt_dtype */
   int32_t causal; /* nonzero: key j is visible to query i only if j <= i */
   float scale;    /* softmax scale; callers map scale=None to 1/sqrt(d) */
+  int32_t window;      /* 0, or (with causal != 0) a band of `window` keys, W: */
+  int32_t window_kind; /* 0 sliding: key j visible to query i iff i - W < j <= i, the
+                          additive mask of cloud_ttt_e2e/ttt_e2e/utils.py:40-54;
+                          1 chunk-local: queries of the full chunk [cW, cW + W) see
+                          keys cW .. i, those of a partial last chunk the last W keys,
+                          the chunk loop of cloud_ttt_e2e/ttt_e2e/attention.py:112-127.
+                          window > 0 without causal returns TTT_ERR_UNSUPPORTED, as do
+                          the P-materializing forward and the from-P passes. */
 } ttt_problem;
 
 /* Forward. Writes o and lse2 (base-2 log-sum-exp of scale*log2(e)*q k^T per

@@ -36,18 +36,41 @@ import numpy as np
 import torch
 
 
-def attention_math(q, k, v, causal: bool, scale: float):
-    """softmax(scale * q k^T, causal triu(1) -> -inf) v  (triton_attention.py:18-25)."""
+def band_visible(t: int, window: int = 0, kind: str = "sliding") -> np.ndarray:
+    """[t, t] bool: key j visible to query i under a causal mask restricted to a band.
+
+    window 0: plain causal (j <= i). kind "sliding": i - window < j <= i, the
+    additive mask of make_window_mask (cloud_ttt_e2e/ttt_e2e/utils.py:40-54).
+    kind "chunk": the attention WindowedSelfAttention computes for t > window
+    with its chunk loop (cloud_ttt_e2e/ttt_e2e/attention.py:112-127): queries of
+    chunk [start, end) see keys max(0, end - window) .. i.
+    """
+    i = np.arange(t)[:, None]
+    j = np.arange(t)[None, :]
+    vis = j <= i
+    if window and kind == "sliding":
+        vis &= (i - j) < window
+    elif window and kind == "chunk":
+        start = (i // window) * window
+        end = np.minimum(t, start + window)
+        vis &= j >= np.maximum(0, end - window)
+    return vis
+
+
+def attention_math(q, k, v, causal: bool, scale: float, window: int = 0, window_kind: str = "sliding"):
+    """softmax(scale * q k^T, causal triu(1) -> -inf) v  (triton_attention.py:18-25);
+    with window > 0 (causal) the mask of band_visible."""
     scores = torch.matmul(q, k.transpose(-2, -1)) * scale
     if causal:
         t = scores.size(-1)
-        mask = torch.triu(torch.ones((t, t), device=scores.device, dtype=torch.bool), diagonal=1)
-        scores = scores.masked_fill(mask, float("-inf"))
+        vis = torch.from_numpy(band_visible(t, window, window_kind)).to(scores.device)
+        scores = scores.masked_fill(~vis, float("-inf"))
     return torch.matmul(torch.softmax(scores, dim=-1), v)
 
 
 def math_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | None = None,
-                  dtype: torch.dtype = torch.float64, need_gdo: bool = False) -> dict:
+                  dtype: torch.dtype = torch.float64, need_gdo: bool = False, window: int = 0,
+                  window_kind: str = "sliding") -> dict:
     """Forward, first-order grads of <O, dO> and second-order grads of
     <dq,uq> + <dk,uk> + <dv,uv>, via torch.autograd on the math path."""
     if scale is None:
@@ -57,7 +80,7 @@ def math_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | None = N
     do_ = cast(do).requires_grad_(need_gdo)
     uq_, uk_, uv_ = cast(uq), cast(uk), cast(uv)
     with torch.enable_grad():
-        o = attention_math(q_, k_, v_, causal, scale)
+        o = attention_math(q_, k_, v_, causal, scale, window, window_kind)
         dq, dk, dv = torch.autograd.grad(o, (q_, k_, v_), do_, create_graph=True)
         l2 = (dq * uq_).sum() + (dk * uk_).sum() + (dv * uv_).sum()
         wrt = (q_, k_, v_, do_) if need_gdo else (q_, k_, v_)
@@ -92,7 +115,8 @@ def _softmax_rows(s: np.ndarray) -> np.ndarray:
     return e / np.sum(e, axis=-1, keepdims=True)
 
 
-def closed_form_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | None = None) -> dict:
+def closed_form_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | None = None, window: int = 0,
+                         window_kind: str = "sliding") -> dict:
     """numpy float64 closed form of the same quantities (see module docstring).
     Inputs are [..., t, d] arrays (any leading batch dims)."""
     q, k, v, do, uq, uk, uv = (np.asarray(x, dtype=np.float64) for x in (q, k, v, do, uq, uk, uv))
@@ -101,8 +125,7 @@ def closed_form_gradgrad(q, k, v, do, uq, uk, uv, causal: bool, scale: float | N
     tr = lambda x: np.swapaxes(x, -1, -2)  # noqa: E731
     s = scale * (q @ tr(k))
     if causal:
-        t = s.shape[-1]
-        s = np.where(np.triu(np.ones((t, t), dtype=bool), 1), -np.inf, s)
+        s = np.where(band_visible(s.shape[-1], window, window_kind), s, -np.inf)
     p = _softmax_rows(s)
     o = p @ v
     dp = do @ tr(v)

@@ -9,7 +9,9 @@ the reference runs its math path (triton_attention.py:275-280 forward,
 416-420 recompute backward). Outputs: forward O, first-order grads of
 <O, dO> (create_graph=True) and second-order grads of <dq,uq>+<dk,uk>+<dv,uv>.
 
-Also records the backward methods of the reference's P-taking autograd
+Also records the reference's TTT-E2E attention (GradGradAttentionFn with a
+sliding-window mask, and WindowedSelfAttention's chunk loop), the backward
+methods of the reference's P-taking autograd
 Functions (TritonDvFn, TritonRowSumFn, TritonDqDkFn) on fixed inputs, and the
 reference's ``save_p`` mode on the same inputs as the math path; its
 grad-grad for q and k differs from the math path because P is saved as a
@@ -114,7 +116,65 @@ def from_p_function_backwards(out_path: Path) -> None:
     print(f"wrote {out_path.name}")
 
 
+def load_reference_ttt_e2e():
+    """The reference's TTT-E2E package (cloud_ttt_e2e/ttt_e2e) under the alias ref_ttt_e2e."""
+    pkg_dir = REF / "cloud_ttt_e2e" / "ttt_e2e"
+    spec = importlib.util.spec_from_file_location("ref_ttt_e2e", pkg_dir / "__init__.py",
+                                                  submodule_search_locations=[str(pkg_dir)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["ref_ttt_e2e"] = mod
+    spec.loader.exec_module(mod)
+    return sys.modules["ref_ttt_e2e.attention"], sys.modules["ref_ttt_e2e.utils"]
+
+
+def ttt_e2e_window_cases(out_path: Path) -> None:
+    """The reference's TTT-E2E attention on CPU (pure torch there):
+    * GradGradAttentionFn.apply(q, k, v, make_window_mask(t, W)) with a binding
+      sliding window (W < t): forward, first-order grads with create_graph and the
+      second-order grads of <dq,uq>+<dk,uk>+<dv,uv>;
+    * WindowedSelfAttention(window_size=W) on a sequence longer than W, so that
+      its chunk loop runs (attention.py:112-127), with a partial last chunk:
+      output, d<out,g>/dx with create_graph, and d<that,u>/dx. Its seeded
+      initial weights are saved with the outputs."""
+    attn, utils = load_reference_ttt_e2e()
+    rec = {}
+    b, h, t, d, w = 1, 2, 48, 16, 12
+    g = torch.Generator().manual_seed(21)
+    x = {n: torch.randn(b, h, t, d, generator=g, dtype=torch.float64) for n in ("q", "k", "v", "do", "uq", "uk", "uv")}
+    q, k, v = (x[n].clone().requires_grad_(True) for n in ("q", "k", "v"))
+    # GradGradAttentionFn keeps a graph only when the upstream gradient requires grad
+    # (need_higher = grad_out.requires_grad, attention.py:32), as in the TTT meta step
+    do = x["do"].clone().requires_grad_(True)
+    mask = utils.make_window_mask(t, w, torch.device("cpu"), torch.float64).view(1, 1, t, t)
+    out = attn.GradGradAttentionFn.apply(q, k, v, mask)
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), do, create_graph=True)
+    l2 = (dq * x["uq"]).sum() + (dk * x["uk"]).sum() + (dv * x["uv"]).sum()
+    gq, gk, gv, gdo = torch.autograd.grad(l2, (q, k, v, do))
+    rec.update({f"sw_in_{n}": t_.numpy() for n, t_ in x.items()})
+    rec.update({f"sw_{n}": t_.detach().numpy() for n, t_ in
+                (("o", out), ("dq", dq), ("dk", dk), ("dv", dv), ("gq", gq), ("gk", gk), ("gv", gv), ("gdo", gdo))})
+    rec["sw_meta"] = np.array([b, h, t, d, w], dtype=np.int64)
+
+    d_model, n_heads, w2, t2 = 32, 2, 16, 40
+    torch.manual_seed(5)
+    mod = attn.WindowedSelfAttention(d_model, n_heads, w2, use_gradgrad=True).double()
+    g2 = torch.Generator().manual_seed(22)
+    xin = torch.randn(1, t2, d_model, generator=g2, dtype=torch.float64).requires_grad_(True)
+    gout = torch.randn(1, t2, d_model, generator=g2, dtype=torch.float64)
+    uin = torch.randn(1, t2, d_model, generator=g2, dtype=torch.float64)
+    y = mod(xin)
+    (gx,) = torch.autograd.grad(y, xin, gout, create_graph=True)
+    (ggx,) = torch.autograd.grad((gx * uin).sum(), xin)
+    rec.update({f"wsa_{n}": p_.detach().numpy() for n, p_ in mod.state_dict().items()})
+    rec.update({"wsa_x": xin.detach().numpy(), "wsa_g": gout.numpy(), "wsa_u": uin.numpy(), "wsa_y": y.detach().numpy(),
+                "wsa_gx": gx.detach().numpy(), "wsa_ggx": ggx.numpy()})
+    rec["wsa_meta"] = np.array([d_model, n_heads, w2, t2], dtype=np.int64)
+    np.savez_compressed(out_path, **rec)
+    print(f"wrote {out_path.name}")
+
+
 def main() -> None:
+    ttt_e2e_window_cases(HERE / "ttt_e2e_windows_fp64.npz")
     ta = load_reference()
     importlib.import_module("ref_ttt_kernels.backward_stubs")
     from_p_function_backwards(HERE / "from_p_function_backwards_t48_d16_fp64.npz")

@@ -45,7 +45,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_host_helpers(lib):
-    assert lib.ttt_attn_abi_version() == 1
+    assert lib.ttt_attn_abi_version() == 2
     assert lib.ttt_attn_t_pad(1) == 128 and lib.ttt_attn_t_pad(128) == 128 and lib.ttt_attn_t_pad(129) == 256
     assert lib.ttt_attn_status_string(0) == b"ok"
     assert b"64 or 128" in lib.ttt_attn_status_string(3)
@@ -105,30 +105,34 @@ def test_kernel_path_rejects_cpu_and_bad_dtypes():
 def _fake_ops(monkeypatch, calls):
     """Replace the kernel ops by oracle-backed CPU functions with the same contract."""
 
-    def fwd(q, k, v, causal, scale, save_p=False):
+    def band(window):
+        w, kind = (window, "sliding") if isinstance(window, int) else window
+        return {"window": w, "window_kind": {"sliding": "sliding", "chunk": "chunk"}[kind]}
+
+    def fwd(q, k, v, causal, scale, save_p=False, window=0):
         calls.append("fwd")
-        out = orc.closed_form_gradgrad(q, k, v, q, q, q, q, causal=causal, scale=scale)
+        out = orc.closed_form_gradgrad(q, k, v, q, q, q, q, causal=causal, scale=scale, **band(window))
         b, h, t, d = q.shape
         lse2 = torch.full((b * h, _lib.t_pad(t)), math.inf, dtype=torch.float32)
         lse2[:, :t] = torch.from_numpy(out["lse"]).reshape(b * h, t).float() / math.log(2.0)
         return torch.from_numpy(out["o"]).to(q.dtype), lse2, None
 
-    def bwd(q, k, v, o, dout, lse2, causal, scale):
+    def bwd(q, k, v, o, dout, lse2, causal, scale, window=0):
         calls.append("bwd")
         out = orc.closed_form_gradgrad(q.detach(), k.detach(), v.detach(), dout.detach(), q.detach(), q.detach(),
-                                       q.detach(), causal=causal, scale=scale)
+                                       q.detach(), causal=causal, scale=scale, **band(window))
         b, h, t, d = q.shape
         delta = torch.zeros((b * h, _lib.t_pad(t)))
         delta[:, :t] = torch.from_numpy(out["delta"]).reshape(b * h, t).float()
         cast = lambda a: torch.from_numpy(a).to(q.dtype)  # noqa: E731
         return cast(out["dq"]), cast(out["dk"]), cast(out["dv"]), delta
 
-    def bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal, scale, need_gdout):
+    def bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal, scale, need_gdout, window=0):
         calls.append("bwd2" + ("+gdo" if need_gdout else ""))
         z = torch.zeros_like(q)
         uq, uk, uv = (z if u is None else u for u in (uq, uk, uv))
         out = orc.closed_form_gradgrad(q.detach(), k.detach(), v.detach(), dout.detach(), uq, uk, uv,
-                                       causal=causal, scale=scale)
+                                       causal=causal, scale=scale, **band(window))
         cast = lambda a: torch.from_numpy(a).to(q.dtype)  # noqa: E731
         return cast(out["gq"]), cast(out["gk"]), cast(out["gv"]), cast(out["gdo"]) if need_gdout else None
 
@@ -212,3 +216,24 @@ def test_dropin_surface_names():
     for name in ("triton_attn_bwd_dv", "triton_attn_bwd_dq", "triton_attn_bwd_dk", "triton_attn_bwd2_dq",
                  "triton_attn_bwd2_dk", "triton_attn_bwd2_dv"):
         assert callable(getattr(backward_stubs, name))
+
+
+@pytest.mark.parametrize("kind", ["sliding", "chunk"])
+def test_band_attention_wiring_matches_oracle(monkeypatch, kind):
+    """ttt_e2e.BandAttentionFn's autograd wiring (forward, differentiable
+    backward, double backward incl. the upstream gradient) on CPU through the
+    same fake kernel ops, against the oracle with the same band."""
+    from testtimeideas_b200 import ttt_e2e
+    calls = []
+    _fake_ops(monkeypatch, calls)
+    inp = orc.seeded_inputs(1, 2, 40, 16, seed=4, scale_in=0.5)
+    q, k, v, do = (inp[n].double().requires_grad_(True) for n in ("q", "k", "v", "do"))
+    out = ttt_e2e.BandAttentionFn.apply(q, k, v, 12, kind)
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), do, create_graph=True)
+    l2 = (dq * inp["uq"]).sum() + (dk * inp["uk"]).sum() + (dv * inp["uv"]).sum()
+    gq, gk, gv, gdo = torch.autograd.grad(l2, (q, k, v, do))
+    ref = orc.math_gradgrad(*(inp[n] for n in ("q", "k", "v", "do", "uq", "uk", "uv")), causal=True, need_gdo=True,
+                            window=12, window_kind=kind)
+    for name, val in (("o", out), ("dq", dq), ("gq", gq), ("gk", gk), ("gv", gv), ("gdo", gdo)):
+        assert orc.normalized_err(val.detach(), ref[name]) < 1e-10, name
+    assert calls == ["fwd", "bwd", "bwd2+gdo"]

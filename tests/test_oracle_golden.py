@@ -17,9 +17,10 @@ import torch
 
 from oracle import attention_oracle as orc
 
-# attention-path cases (the P-taking Function fixture is covered by test_from_p_cpu.py)
+# attention-path cases (the P-taking Function fixture is covered by test_from_p_cpu.py,
+# the TTT-E2E window fixture by test_ttt_e2e_cpu.py)
 GOLDEN = sorted(p for p in glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz"))
-                if not os.path.basename(p).startswith("from_p_"))
+                if not os.path.basename(p).startswith(("from_p_", "ttt_e2e_")))
 NAMES = ("q", "k", "v", "do", "uq", "uk", "uv")
 
 

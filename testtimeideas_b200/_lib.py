@@ -31,7 +31,8 @@ class View(ctypes.Structure):
 
 class Problem(ctypes.Structure):
     _fields_ = [("b", ctypes.c_int32), ("h", ctypes.c_int32), ("t", ctypes.c_int32), ("d", ctypes.c_int32),
-                ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_float)]
+                ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_float),
+                ("window", ctypes.c_int32), ("window_kind", ctypes.c_int32)]
 
 
 class FwdArgs(ctypes.Structure):
@@ -173,9 +174,15 @@ def view(x: torch.Tensor | None) -> View:
     return View(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2))
 
 
-def problem(q: torch.Tensor, causal: bool, scale: float) -> Problem:
+WINDOW_KINDS = {"sliding": 0, "chunk": 1}
+
+
+def problem(q: torch.Tensor, causal: bool, scale: float, window=0) -> Problem:
+    """window: 0, an int W (sliding: key j visible to query i iff i - W < j <= i) or
+    a (W, kind) pair with kind "sliding" or "chunk" (chunk-local, see include/ttt_attn.h)."""
     b, h, t, d = q.shape
-    return Problem(b, h, t, d, _dtype_code(q), 1 if causal else 0, float(scale))
+    w, kind = (window, "sliding") if isinstance(window, int) else window
+    return Problem(b, h, t, d, _dtype_code(q), 1 if causal else 0, float(scale), int(w), WINDOW_KINDS[kind])
 
 
 def validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -202,7 +209,7 @@ def default_scale(d: int) -> float:
 
 
 # ---------------------------------------------------------------- ops
-def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False):
+def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: int = 0):
     """O, lse2 (fp32 [b*h, t_pad]) and, with save_p, P ([b, h, t, t])."""
     validate(q, k, v)
     lib = load_library()
@@ -213,7 +220,7 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False):
         lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         # causal: the kernel writes only key tiles up to the diagonal; the rest stays zero
         p = (torch.zeros if causal else torch.empty)((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
-        args = FwdArgs(problem(q, causal, scale), view(q), view(k), view(v), view(o), lse2.data_ptr(),
+        args = FwdArgs(problem(q, causal, scale, window), view(q), view(k), view(v), view(o), lse2.data_ptr(),
                        p.data_ptr() if p is not None else None, error_word(q.device).data_ptr())
         _check(lib.ttt_attn_fwd(ctypes.byref(args), _stream()))
         if _SYNC_CHECK:
@@ -221,7 +228,7 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False):
     return o, lse2, p
 
 
-def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float):
+def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0):
     """dq, dk, dv and delta = rowsum(dout o o) (fp32 [b*h, t_pad])."""
     validate(q, k, v)
     lib = load_library()
@@ -230,7 +237,7 @@ def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float):
     with torch.cuda.device(q.device):
         dq, dk, dv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
         delta = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
-        args = BwdArgs(problem(q, causal, scale), view(q), view(k), view(v), view(o), view(dout),
+        args = BwdArgs(problem(q, causal, scale, window), view(q), view(k), view(v), view(o), view(dout),
                        lse2.data_ptr(), delta.data_ptr(), view(dq), view(dk), view(dv),
                        error_word(q.device).data_ptr())
         _check(lib.ttt_attn_bwd(ctypes.byref(args), _stream()))
@@ -239,7 +246,8 @@ def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float):
     return dq, dk, dv, delta
 
 
-def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float, need_gdout: bool):
+def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float, need_gdout: bool,
+              window: int = 0):
     """Second-order gradients gq, gk, gv (and gdout when requested, else None)."""
     validate(q, k, v)
     lib = load_library()
@@ -261,7 +269,7 @@ def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float
         gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
         gamma = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         rho = torch.empty_like(gamma)
-        args = Bwd2Args(problem(q, causal, scale), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
+        args = Bwd2Args(problem(q, causal, scale, window), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
                         delta.data_ptr(), view(uq), view(uk), view(uv), gamma.data_ptr(), rho.data_ptr(),
                         view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr())
         _check(lib.ttt_attn_bwd2(ctypes.byref(args), _stream()))

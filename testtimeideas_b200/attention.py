@@ -60,11 +60,12 @@ class _AttnBwdFn(torch.autograd.Function):
     backward = the complete double backward (grads w.r.t. q, k, v and dO)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, dout, o, lse2, causal: bool, scale: float):
-        dq, dk, dv, delta = _lib.attn_bwd(q, k, v, o, dout, lse2, causal, scale)
+    def forward(ctx, q, k, v, dout, o, lse2, causal: bool, scale: float, window=0):
+        dq, dk, dv, delta = _lib.attn_bwd(q, k, v, o, dout, lse2, causal, scale, window=window)
         ctx.save_for_backward(q, k, v, dout, lse2, delta)
         ctx.causal = causal
         ctx.scale = scale
+        ctx.window = window
         return dq, dk, dv
 
     @staticmethod
@@ -72,8 +73,9 @@ class _AttnBwdFn(torch.autograd.Function):
     def backward(ctx, gdq, gdk, gdv):
         q, k, v, dout, lse2, delta = ctx.saved_tensors
         need_gdo = bool(ctx.needs_input_grad[3])
-        gq, gk, gv, gdo = _lib.attn_bwd2(q, k, v, dout, lse2, delta, gdq, gdk, gdv, ctx.causal, ctx.scale, need_gdo)
-        return gq, gk, gv, gdo, None, None, None, None
+        gq, gk, gv, gdo = _lib.attn_bwd2(q, k, v, dout, lse2, delta, gdq, gdk, gdv, ctx.causal, ctx.scale, need_gdo,
+                                         window=ctx.window)
+        return gq, gk, gv, gdo, None, None, None, None, None
 
 
 class TritonAttentionFn(torch.autograd.Function):

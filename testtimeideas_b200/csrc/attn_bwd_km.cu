@@ -131,11 +131,15 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   uint64_t* l_empty = bars + 5;   // [4]
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_free = bars + 11;   // [2] (NCT arrivals)
-  uint64_t* e_full = bars + 13;   // NCT arrivals
-  uint64_t* e_empty = bars + 14;  // accumulate products of a tile finished (E consumed)
-  uint64_t* acc_full = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint64_t* e_done = bars + 17;   // MMA thread's own wait point for E_OVERLAP
+  // e_full[n % 2] (NCT arrivals): E of tile n written. Two barriers, because a
+  // compute warp may finish tile n+1 before a slower one finishes tile n; with
+  // one barrier its second arrival would complete tile n's phase early. It
+  // cannot reach tile n+2 before tile n's phase completed: those scores are
+  // issued only after the MMA thread has seen e_full for tile n.
+  uint64_t* e_full = bars + 13;   // [2]
+  uint64_t* e_empty = bars + 15;  // accumulate products of a tile finished (E consumed)
+  uint64_t* acc_full = bars + 16;
+  uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto tileR = [&](int t) { return sR + t * C::TILE_R; };
@@ -152,14 +156,19 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const int k0 = kblk * BK;
   const int T = p.T;
   const int n_q = (T + BM - 1) / BM;
+  // Causal: this key block meets query tiles from its diagonal up to the last
+  // query that sees its last key.
+  const Band band = Band::make(p, CAUSAL);
   const int qt0 = CAUSAL ? (k0 / BM) : 0;
-  const int n_tiles = n_q - qt0;
+  const int qt_end = CAUSAL ? min(n_q, band.last_query(min(k0 + BK, T) - 1) / BM + 1) : n_q;
+  const int n_tiles = qt_end - qt0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
-    mbar_init(e_full, C::NCT);
+    mbar_init(e_full + 0, C::NCT);
+    mbar_init(e_full + 1, C::NCT);
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
     fence_mbar_init();
@@ -307,8 +316,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         const bool need_s = nxt && n + 1 >= NBUF;
         const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
         const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
-        const uint64_t* be = n >= 1 ? e_full : done;
-        const uint32_t pe = n >= 1 ? (n - 1) & 1 : 0u;
+        const uint64_t* be = n >= 1 ? e_full + ((n - 1) & 1) : done;
+        const uint32_t pe = n >= 1 ? ((n - 1) >> 1) & 1 : 0u;
         bool next_l = false, next_s = false, seen_e = false;
         if (has_scores) {
           if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
@@ -322,7 +331,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         }
         if (n >= 1) {
           // accumulate products of tile n-1
-          if (!seen_e && !(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
+          if (!seen_e && !(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
           tc_fence_after();
           const uint32_t seen = acc_products(n - 1, bl, pl, bs, ps);
           if constexpr (C::E_DEDICATED) umma_commit(e_empty);
@@ -356,6 +365,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float c = p.scale_log2, scale = p.scale;
     const bool key_edge = k0 + BK > T;
+    // last query that sees this thread's key: key <= qi <= key_hi (the band's dual form)
+    const int key_hi = band.last_query(key);
+    // query tiles ending past the last query that sees the block's first key need the band mask
+    const int band_last = CAUSAL ? band.last_query(k0) : 0x3fffffff;
     const F2 C2 = f2s(c), SC2 = f2s(scale);
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
@@ -385,7 +398,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       tc_fence_before();
       mbar_arrive(s_free + sb);
 
-      const bool need_mask = key_edge || (CAUSAL && qt * BM < k0 + BK - 1);
+      const bool need_mask = key_edge || (CAUSAL && (qt * BM < k0 + BK - 1 || qt * BM + BM - 1 > band_last));
       const float4* st_lse = reinterpret_cast<const float4*>(statS(s, 0) + c0);
       const float4* st_del = reinterpret_cast<const float4*>(statS(s, 1) + c0);
       const float4* st_gam = reinterpret_cast<const float4*>(statS(s, C::BWD2 ? 2 : 0) + c0);
@@ -408,8 +421,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           if (need_mask) {
             const int qi = qcol0 + e;
-            p0 = ((key < T) && (!CAUSAL || key <= qi)) ? p0 : 0.f;
-            p1 = ((key < T) && (!CAUSAL || key <= qi + 1)) ? p1 : 0.f;
+            p0 = ((key < T) && (!CAUSAL || (key <= qi && qi <= key_hi))) ? p0 : 0.f;
+            p1 = ((key < T) && (!CAUSAL || (key <= qi + 1 && qi + 1 <= key_hi))) ? p1 : 0.f;
           }
           const F2 PR = f2(p0, p1), DP = f2(dp[e], dp[e + 1]);
           if constexpr (!C::BWD2) {
@@ -455,7 +468,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         tmem_wait_st();
         tc_fence_before();
       }
-      mbar_arrive(e_full);
+      mbar_arrive(e_full + (n & 1));
     }
     if (ok && mbar_wait(acc_full, 0, g, 8)) {
       tc_fence_after();

@@ -80,7 +80,7 @@ struct QmCfg {
   static constexpr int OFF_S = OFF_R + NR_SMEM * TILE_R;
   static constexpr int OFF_E = OFF_S + NSTAGE * STAGE;
   static constexpr int OFF_BAR = OFF_E + E_BYTES;
-  static constexpr int NBAR = 16;
+  static constexpr int NBAR = 17;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "query-major tile set exceeds shared memory");
   // TMEM column offsets of the score tiles within one buffer
@@ -109,13 +109,18 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   uint64_t* l_empty = bars + 5;  // [4] MMA -> TMA
   uint64_t* s_full = bars + 9;   // [2] MMA -> compute
   uint64_t* s_free = bars + 11;  // [2] compute -> MMA (NCT arrivals)
-  uint64_t* e_full = bars + 13;  // compute -> MMA (NCT arrivals)
-  uint64_t* e_empty = bars + 14; // MMA -> compute
-  uint64_t* acc_full = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  // e_full[n % 2] (NCT arrivals): E of tile n written. Two barriers, because a
+  // compute warp may finish tile n+1 before a slower one finishes tile n; with
+  // one barrier its second arrival would complete tile n's phase early. It
+  // cannot reach tile n+2 before tile n's phase completed: those scores are
+  // issued only after the MMA thread has seen e_full for tile n.
+  uint64_t* e_full = bars + 13;  // [2] compute -> MMA
+  uint64_t* e_empty = bars + 15; // MMA -> compute
+  uint64_t* acc_full = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  static_assert(17 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
+  static_assert(18 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
   // resident tiles kept in shared memory, packed in slot order
   auto in_tmem = [&](int t) { return (t == 0 && C::RT_Q) || (t == 1 && C::RT_DO) || (t == 2 && C::RT_UQ); };
   auto tileR = [&](int t) {
@@ -133,13 +138,17 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const int q0 = qblk * BM;
   const int T = p.T;
   const int n_all = (T + BN - 1) / BN;
-  const int n_tiles = CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all;
+  // Causal: key tiles before the first row's band, or past the diagonal, are skipped.
+  const Band band = Band::make(p, CAUSAL);
+  const int n_first = CAUSAL ? band.lo(q0) / BN : 0;  // first key tile visited
+  const int n_tiles = (CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all) - n_first;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 17; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
-    mbar_init(e_full, C::NCT);
+    mbar_init(e_full + 0, C::NCT);
+    mbar_init(e_full + 1, C::NCT);
     if (C::RES_TMEM) mbar_init(res_full, 1 + C::NCT);  // TMA + the compute warps' copies into TMEM
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
@@ -184,7 +193,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         for (int t = 0; t < NSTR; ++t) {
           uint8_t* dst = tileS(s, t & 1) + (t >> 1) * BN * 128;
           for (int pp = 0; pp < NP; ++pp)
-            tma_load_4d(dst + pp * SR * 128, &p.str[t], l_full + s, pp * 64, n * BN, hidx, bidx);
+            tma_load_4d(dst + pp * SR * 128, &p.str[t], l_full + s, pp * 64, (n_first + n) * BN, hidx, bidx);
         }
         issued[s] = n + 1;
       }
@@ -300,8 +309,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
         if (C::NA > 0 && n >= 1) {
           // tile n-1's accumulate step follows: probe its e_full while issuing these scores
-          const uint32_t seen = issue_scores(n, e_full, (n - 1) & 1, bl, pl);
-          if (!(seen & 1) && !(ok = mbar_wait(e_full, (n - 1) & 1, g, 4))) break;
+          uint64_t* be = e_full + ((n - 1) & 1);
+          const uint32_t pe = ((n - 1) >> 1) & 1;
+          const uint32_t seen = issue_scores(n, be, pe, bl, pl);
+          if (!(seen & 1) && !(ok = mbar_wait(be, pe, g, 4))) break;
           tc_fence_after();
           const uint32_t seen2 = issue_acc(n - 1, bl, pl, bs, ps);
           have_l = ((seen >> 1) & 1) || (seen2 & 1);
@@ -314,7 +325,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       }
       if constexpr (C::NA > 0) {
         if (ok && n_tiles > 0) {
-          ok = mbar_wait(e_full, (n_tiles - 1) & 1, g, 4);
+          ok = mbar_wait(e_full + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, g, 4);
           if (ok) {
             tc_fence_after();
             issue_acc(n_tiles - 1, done, 0u, done, 0u);
@@ -333,6 +344,8 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     const int c0 = half * CPW;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int64_t sidx = static_cast<int64_t>(bh) * p.t_pad + row;
+    const int row_lo = band.lo(row);
+    const int band_edge = CAUSAL ? band.lo(q0 + BM - 1) : 0;  // tiles starting before it need the band mask
     const float c = p.scale_log2, scale = p.scale;
     const float lse = p.lse2[sidx];
     const float del = p.delta[sidx];
@@ -397,8 +410,9 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       tc_fence_before();
       mbar_arrive(s_free + sb);  // scores are in registers: the next tile's products may overwrite them
 
-      const int j0 = n * BN + c0;
-      const bool need_mask = (n * BN + BN > T) || (CAUSAL && n * BN + BN - 1 > q0);
+      const int kt0 = (n_first + n) * BN;  // first key of the tile
+      const int j0 = kt0 + c0;
+      const bool need_mask = (kt0 + BN > T) || (CAUSAL && (kt0 + BN - 1 > q0 || band_edge > kt0));
 #pragma unroll
       for (int e = 0; e < CPW; e += 2) {
         float x0, x1;
@@ -406,8 +420,8 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
         if (need_mask) {
           const int j = j0 + e;
-          p0 = ((j < T) && (!CAUSAL || j <= row)) ? p0 : 0.f;
-          p1 = ((j + 1 < T) && (!CAUSAL || j + 1 <= row)) ? p1 : 0.f;
+          p0 = ((j < T) && (!CAUSAL || (j <= row && j >= row_lo))) ? p0 : 0.f;
+          p1 = ((j + 1 < T) && (!CAUSAL || (j + 1 <= row && j + 1 >= row_lo))) ? p1 : 0.f;
         }
         const F2 PR = f2(p0, p1), DP = f2(dp[e], dp[e + 1]);
         if constexpr (KIND == kBwdQ) {
@@ -444,7 +458,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
           }
         }
         fence_async_smem();
-        mbar_arrive(e_full);
+        mbar_arrive(e_full + (n & 1));
       }
     }
     const bool valid = row < T;

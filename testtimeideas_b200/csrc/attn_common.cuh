@@ -50,9 +50,44 @@ struct KParams {
   uint16_t* out1;
   int64_t o1_sb, o1_sh, o1_st;
   int B, H, T, t_pad;
+  int window;        // causal only, 0 = none: see Band
+  int window_kind;   // 0 sliding window, 1 chunk-local (see Band)
   float scale;       // softmax scale applied to Q K^T
   float scale_log2;  // scale * log2(e)
   int* err;          // device error word (0 = ok), may be null
+};
+
+// Causal attention with a lower bound on each row's visible keys: key j is
+// visible to query i iff lo(i) <= j <= i. Kinds:
+//   none          lo(i) = 0
+//   sliding       lo(i) = max(0, i - W + 1)   (an additive mask from
+//                 make_window_mask, cloud_ttt_e2e/ttt_e2e/utils.py:40-54)
+//   chunk-local   queries in full chunks [cW, cW + W) see keys from cW; the
+//                 queries of a last partial chunk see the last W keys: the
+//                 chunk loop of WindowedSelfAttention for T > W
+//                 (cloud_ttt_e2e/ttt_e2e/attention.py:112-127)
+// lo is non-decreasing in i and last_query (the last query seeing key j) in j.
+struct Band {
+  int kind;  // 0 none, 1 sliding, 2 chunk-local
+  int W, T, tf;  // tf = start of a partial last chunk (= T when there is none)
+  TTT_DEV static Band make(const KParams& p, bool causal) {
+    Band b;
+    b.kind = (causal && p.window > 0) ? 1 + p.window_kind : 0;
+    b.W = p.window > 0 ? p.window : 1;
+    b.T = p.T;
+    b.tf = (p.T / b.W) * b.W;
+    return b;
+  }
+  TTT_DEV int lo(int i) const {
+    if (kind == 1) return max(0, i - W + 1);
+    if (kind == 2) return i < tf ? (i / W) * W : max(0, T - W);
+    return 0;
+  }
+  TTT_DEV int last_query(int j) const {
+    if (kind == 1) return j + W - 1;
+    if (kind == 2) return (tf < T && j >= T - W) ? T - 1 : (j / W + 1) * W - 1;
+    return 0x3fffffff;
+  }
 };
 
 // Dynamic shared memory is only guaranteed 16-byte aligned; the 128-byte

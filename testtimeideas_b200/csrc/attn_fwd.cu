@@ -364,11 +364,19 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
   const int q0 = blk * 2 * BM;
   const int T = p.T;
   const int n_all = (T + BN - 1) / BN;
-  // key tiles visited by query tile w (none when the tile starts past the sequence)
+  // Key tiles [lo_w, hi_w) visited by query tile w (none when the tile starts
+  // past the sequence). Causal: tiles before the band of the tile's first row
+  // and past its diagonal are skipped.
+  const Band band = Band::make(p, CAUSAL);
   const int qs0 = q0, qs1 = q0 + BM;
-  const int nt0 = qs0 >= T ? 0 : (CAUSAL ? min(n_all, qs0 / BN + 1) : n_all);
-  const int nt1 = qs1 >= T ? 0 : (CAUSAL ? min(n_all, qs1 / BN + 1) : n_all);
-  const int n_kv = max(nt0, nt1);
+  const int hi0 = qs0 >= T ? 0 : (CAUSAL ? min(n_all, qs0 / BN + 1) : n_all);
+  const int hi1 = qs1 >= T ? 0 : (CAUSAL ? min(n_all, qs1 / BN + 1) : n_all);
+  const int lo0 = CAUSAL ? band.lo(qs0) / BN : 0;
+  const int lo1 = CAUSAL ? band.lo(min(qs1, T - 1)) / BN : 0;
+  const int nt0 = max(0, hi0 - lo0), nt1 = max(0, hi1 - lo1);
+  // the CTA streams key tiles n_lo .. n_lo + n_kv - 1 (relative index r = n - n_lo)
+  const int n_lo = lo0;
+  const int n_kv = max(hi0, nt1 > 0 ? hi1 : 0) - n_lo;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NBAR; ++i) mbar_init(bars + i, 1);
@@ -403,13 +411,14 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
       int n = 0;
       for (; n < n_kv; ++n) {
         const int s = n % NS;
+        const int key0 = (n_lo + n) * BN;
         if (n >= NS && !mbar_wait(kv_empty + s, ((n / NS) - 1) & 1, g, 1)) break;
         mbar_arrive_tx(k_full + s, C::TILE_KV);
         for (int pp = 0; pp < NP; ++pp)
-          tma_load_4d(sK + s * C::TILE_KV + pp * BN * 128, &p.str[0], k_full + s, pp * 64, n * BN, hidx, bidx);
+          tma_load_4d(sK + s * C::TILE_KV + pp * BN * 128, &p.str[0], k_full + s, pp * 64, key0, hidx, bidx);
         mbar_arrive_tx(v_full + s, C::TILE_KV);
         for (int pp = 0; pp < NP; ++pp)
-          tma_load_4d(sV + s * C::TILE_KV + pp * BN * 128, &p.str[1], v_full + s, pp * 64, n * BN, hidx, bidx);
+          tma_load_4d(sV + s * C::TILE_KV + pp * BN * 128, &p.str[1], v_full + s, pp * 64, key0, hidx, bidx);
       }
       // Wait for every load this thread issued before the CTA may exit.
       mbar_drain(q_full, 0);
@@ -423,7 +432,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(128, BN, BF16, false, false);
       constexpr uint32_t id_o = idesc_f16(128, D, BF16, false, true);
-      const int nt[2] = {nt0, nt1};
+      // query tile w takes part in relative steps [first[w], first[w] + nt[w])
+      const int first[2] = {lo0 - n_lo, lo1 - n_lo}, nt[2] = {nt0, nt1};
       int k_seen = 0;  // key tiles whose K load this thread has waited for
       bool ok = mbar_wait(q_full, 0, g, 2);
       auto wait_k = [&](int n) -> bool {
@@ -441,23 +451,25 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
         umma_commit(s_full + w);
       };
       if (ok && n_kv > 0 && (ok = wait_k(0))) {
-        if (nt0 > 0) issue_s(0, 0);
-        if (nt1 > 0) issue_s(1, 0);
+        for (int w = 0; w < 2; ++w)
+          if (first[w] == 0 && nt[w] > 0) issue_s(w, 0);
       }
       for (int n = 0; ok && n < n_kv; ++n) {
         const int s = n % NS;
         if (!(ok = mbar_wait(v_full + s, (n / NS) & 1, g, 4))) break;
         const uint32_t bv = smem_u32(sV + s * C::TILE_KV);
         for (int w = 0; w < 2 && ok; ++w) {
-          if (n >= nt[w]) continue;
-          if (!(ok = mbar_wait(p_full + w, n & 1, g, 5))) break;
-          tc_fence_after();
-          const uint32_t tP = tmem + w * 128, tO = tmem + 256 + w * D;
+          const int i = n - first[w];  // this query tile's own step index
+          if (i >= 0 && i < nt[w]) {
+            if (!(ok = mbar_wait(p_full + w, i & 1, g, 5))) break;
+            tc_fence_after();
+            const uint32_t tP = tmem + w * 128, tO = tmem + 256 + w * D;
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ts(tO, tP + kk * 8, desc_mnmajor(bv, BN, kk), id_o, (n > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(pv_done + w);
-          if (n + 1 < nt[w]) {
+            for (int kk = 0; kk < BN / 16; ++kk)
+              umma_ts(tO, tP + kk * 8, desc_mnmajor(bv, BN, kk), id_o, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(pv_done + w);
+          }
+          if (i + 1 >= 0 && i + 1 < nt[w]) {
             if (!(ok = wait_k(n + 1))) break;
             issue_s(w, n + 1);
           }
@@ -475,11 +487,15 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
     const int r = quarter * 32 + lane;
     const int row = q0 + w * BM + r;
     const int ntw = w ? nt1 : nt0;
+    const int low = w ? lo1 : lo0;  // first key tile of this query tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + w * 128;
     const uint32_t tO = tmem + lane_off + 256 + w * D;
     const float c = p.scale_log2;
     const int qw0 = q0 + w * BM;
+    const int row_lo = band.lo(row);
+    // key tiles from this one on are fully visible to the whole query tile (below the diagonal)
+    const int band_edge = CAUSAL ? band.lo(qw0 + BM - 1) : 0;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int n = 0; n < ntw; ++n) {
@@ -490,12 +506,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
       tmem_ld_nw<64>(tS + 64, *reinterpret_cast<float(*)[64]>(sv + 64));
       tmem_wait_ld();
       reg_fence(sv);
-      const int k0 = n * BN;
-      if ((k0 + BN > T) || (CAUSAL && k0 + BN - 1 > qw0)) {
+      const int k0 = (low + n) * BN;
+      if ((k0 + BN > T) || (CAUSAL && (k0 + BN - 1 > qw0 || band_edge > k0))) {
 #pragma unroll
         for (int j = 0; j < BN; ++j) {
           const int col = k0 + j;
-          sv[j] = ((col < T) && (!CAUSAL || col <= row)) ? sv[j] : -INFINITY;
+          sv[j] = ((col < T) && (!CAUSAL || (col <= row && col >= row_lo))) ? sv[j] : -INFINITY;
         }
       }
       float mx8[8];
@@ -527,7 +543,9 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
           }
         }
       }
-      const F2 C2 = f2s(c), NM = f2s(-m_used);
+      // A row whose window has not started yet has no visible key so far (m_used = -inf):
+      // its P is 0, and the exponent offset must stay finite.
+      const F2 C2 = f2s(c), NM = f2s(m_used == -INFINITY ? 0.f : -m_used);
       F2 acc[4] = {f2s(0.f), f2s(0.f), f2s(0.f), f2s(0.f)};
 #pragma unroll
       for (int q = 0; q < BN / 32; ++q) {

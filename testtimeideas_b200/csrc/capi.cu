@@ -39,6 +39,9 @@ int check_problem(const ttt_problem& pb) {
   if (pb.b < 1 || pb.h < 1 || pb.t < 1) return TTT_ERR_SHAPE;
   if (pb.t > (1 << 22)) return TTT_ERR_SHAPE;
   if (static_cast<int64_t>(pb.b) * pb.h > 0x7fffffff) return TTT_ERR_SHAPE;
+  if (pb.window < 0) return TTT_ERR_SHAPE;
+  if (pb.window > 0 && pb.causal == 0) return TTT_ERR_UNSUPPORTED;
+  if (pb.window_kind != 0 && pb.window_kind != 1) return TTT_ERR_UNSUPPORTED;
   return TTT_OK;
 }
 
@@ -139,6 +142,8 @@ void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
   k.T = pb.t;
   k.t_pad = ttt_attn_t_pad(pb.t);
   k.scale = pb.scale;
+  k.window = pb.causal != 0 ? pb.window : 0;
+  k.window_kind = pb.window_kind;
   k.scale_log2 = pb.scale * 1.4426950408889634f;
   k.err = err;
 }
@@ -257,6 +262,7 @@ int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
   TTT_TRY(check_view(a->o, pb));
   TTT_TRY(check_stats(a->lse2));
   if (a->p != nullptr && !aligned16(a->p)) return TTT_ERR_ALIGN;
+  if (a->p != nullptr && pb.window > 0) return TTT_ERR_UNSUPPORTED;
   KParams k;
   std::memset(&k, 0, sizeof(k));
   fill_common(k, pb, a->err);
@@ -426,6 +432,7 @@ int ttt_attn_dv_from_p(const ttt_from_p_args* a, void* stream) {
   if (a == nullptr) return TTT_ERR_NULL;
   const ttt_problem& pb = a->pb;
   TTT_TRY(check_problem(pb));
+  if (pb.window > 0) return TTT_ERR_UNSUPPORTED;
   TTT_TRY(check_p_view(a->p, pb));
   TTT_TRY(check_view(a->dout, pb));
   TTT_TRY(check_view(a->dv, pb));
@@ -444,6 +451,7 @@ int ttt_attn_rowsum_from_p(const ttt_from_p_args* a, void* stream) {
   if (a == nullptr) return TTT_ERR_NULL;
   const ttt_problem& pb = a->pb;
   TTT_TRY(check_problem(pb));
+  if (pb.window > 0) return TTT_ERR_UNSUPPORTED;
   TTT_TRY(check_p_view(a->p, pb));
   TTT_TRY(check_view(a->dout, pb));
   TTT_TRY(check_view(a->v, pb));
@@ -464,6 +472,7 @@ int ttt_attn_dqdk_from_p(const ttt_from_p_args* a, void* stream) {
   if (a == nullptr) return TTT_ERR_NULL;
   const ttt_problem& pb = a->pb;
   TTT_TRY(check_problem(pb));
+  if (pb.window > 0) return TTT_ERR_UNSUPPORTED;
   TTT_TRY(check_p_view(a->p, pb));
   const ttt_view* views[] = {&a->q, &a->k, &a->v, &a->dout, &a->dq, &a->dk};
   for (const ttt_view* v : views) TTT_TRY(check_view(*v, pb));
