@@ -62,6 +62,13 @@ CONFIGS = {
     "c2pc": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=True, scale_in=0.5, step="from_p", flush=True,
                  workload="BASELINE config 2: fwd (P written) + first-order backward from P "
                           "(dv/rowsum/dq+dk from P) b=2 h=4 T=2048 d=128 fp16 causal"),
+    # the TTT-E2E meta step (one inner SGD step with create_graph, outer loss backward)
+    "c5": dict(b=1, h=12, t=8192, d=64, dtype="bf16", causal=True, scale_in=1.0, step="meta",
+               model=dict(n_layers=12, d_model=768, n_heads=12, d_ff=3072, vocab_size=32000, max_seq_len=8192,
+                          window_size=None),
+               workload="BASELINE config 5: TTT-E2E meta step, 12 layers d_model=768 12 heads d_ff=3072 vocab 32000, "
+                        "bf16, b=1 T=8192, inner_steps=1 inner_lr=0.01 on the first 6144 tokens, outer loss on the "
+                        "last 2048, all parameters updated, attention on the kernels"),
     "c8p": dict(b=1, h=8, t=8192, d=128, dtype="fp16", causal=False, scale_in=0.5, step="from_p",
                 workload="fwd (P written) + first-order backward from P, b=1 h=8 T=8192 d=128 fp16 "
                          "non-causal (P = 1 GiB, larger than L2)"),
@@ -262,6 +269,77 @@ def step_fn(cfg: dict):
 STEP_INPUTS = {"gradgrad": ("q", "k", "v", "do", "uq", "uk", "uv"), "from_p": ("q", "k", "v", "do")}
 
 
+def run_meta(args, cfg: dict) -> None:
+    """Config 5: one TTT-E2E meta step per timed step (meta_step + outer backward) on one GPU.
+    value = tokens per second; the attention kernels' share comes from the profiling hook."""
+    from testtimeideas_b200 import _lib, ttt_model
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("the meta-step workload runs on one GPU")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    mcfg = ttt_model.ModelConfig(**cfg["model"])
+    torch.manual_seed(0)
+    model = ttt_model.TTTModel(mcfg).to(device, torch.bfloat16)
+    t, ctx = cfg["t"], 3 * cfg["t"] // 4
+    g = torch.Generator(device=device).manual_seed(1)
+    ids = torch.randint(0, mcfg.vocab_size, (1, t), generator=g, device=device)
+    tgt = torch.randint(0, mcfg.vocab_size, (1, t), generator=g, device=device)
+    inner_mask = torch.zeros(1, t, device=device)
+    inner_mask[:, :ctx] = 1.0
+    outer_mask = 1.0 - inner_mask
+
+    def step(a, b_, im, om):
+        model.zero_grad(set_to_none=True)
+        inner, outer = ttt_model.meta_step(model, a, b_, im, om, inner_lr=0.01, inner_steps=1)
+        outer.backward()
+        return outer.detach()
+
+    for _ in range(args.warmup):
+        step(ids, tgt, inner_mask, outer_mask)
+    _lib.check_device_errors(device)
+    clocks = ClockSampler(0)
+    torch.cuda.synchronize(device)
+    _lib.profile_collect()
+    _lib.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(ids, tgt, inner_mask, outer_mask)
+    e1.record()
+    torch.cuda.synchronize(device)
+    _lib.profile_enable(False)
+    prof = _lib.profile_collect()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: token ids and masks from pinned host memory, the outer loss back
+    host = [x.cpu().pin_memory() for x in (ids, tgt, inner_mask, outer_mask)]
+    dev = [torch.empty_like(x) for x in (ids, tgt, inner_mask, outer_mask)]
+    loss_host = torch.empty((), dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize(device)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        for d_, h_ in zip(dev, host):
+            d_.copy_(h_, non_blocking=True)
+        loss_host.copy_(step(*dev), non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    kern = {k: v for k, v in prof.items() if v[0] > 0}
+    attn_ms = sum(v[1] for v in kern.values()) / args.steps
+    line = {"metric": "TTT-E2E meta step tokens/s (config 5)", "value": t / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform token ids)",
+            "config": {"workload": cfg["workload"], "t": t, "l2": "activations far larger than L2"},
+            "e2e": {"value": t / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host),
+                    "d2h_bytes_per_step": loss_host.element_size()},
+            "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms,
+            "kernel_ms_per_step": {k: v[1] / args.steps for k, v in kern.items()},
+            "gpu_launches": sum(v[0] for v in kern.values()), "clocks": clk, "roofline": None, "cpu_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, cfg: dict) -> None:
     from testtimeideas_b200 import _lib
     from testtimeideas_b200.sharding import head_range, max_over_ranks as _max_over_ranks
@@ -449,6 +527,8 @@ def main() -> None:
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif cfg.get("step") == "meta":
+        run_meta(args, cfg)
     else:
         run_ours(args, cfg)
 

@@ -10,7 +10,8 @@ the reference runs its math path (triton_attention.py:275-280 forward,
 <O, dO> (create_graph=True) and second-order grads of <dq,uq>+<dk,uk>+<dv,uv>.
 
 Also records the reference's TTT-E2E attention (GradGradAttentionFn with a
-sliding-window mask, and WindowedSelfAttention's chunk loop), the backward
+sliding-window mask, and WindowedSelfAttention's chunk loop) and meta step on
+tiny models, the backward
 methods of the reference's P-taking autograd
 Functions (TritonDvFn, TritonRowSumFn, TritonDqDkFn) on fixed inputs, and the
 reference's ``save_p`` mode on the same inputs as the math path; its
@@ -173,8 +174,45 @@ def ttt_e2e_window_cases(out_path: Path) -> None:
     print(f"wrote {out_path.name}")
 
 
+# (name, cfg overrides, t, inner_steps, inner_lr, param_filter, chunk_size)
+META_CASES = [
+    ("meta_full", dict(window_size=None, suffix_layers=-1), 24, 1, 0.1, None, None),
+    ("meta_chunked", dict(window_size=8, suffix_layers=1), 24, 2, 0.05, "mlp_fast", 12),
+]
+
+
+def ttt_e2e_meta_cases(out_path: Path) -> None:
+    """The reference's meta_step (cloud_ttt_e2e/ttt_e2e/meta.py:148-184) on tiny
+    float64 TTT models on CPU: inner and outer losses and the meta-gradient
+    (d outer_loss / d every parameter), with the seeded initial weights."""
+    load_reference_ttt_e2e()
+    model_mod, meta_mod = sys.modules["ref_ttt_e2e.model"], sys.modules["ref_ttt_e2e.meta"]
+    rec = {}
+    for name, over, t, steps, lr, pfilter, chunk in META_CASES:
+        cfg = model_mod.ModelConfig(vocab_size=64, max_seq_len=64, d_model=32, n_heads=2, n_layers=2, d_ff=64,
+                                    **over)
+        torch.manual_seed(11)
+        model = model_mod.TTTModel(cfg).double()
+        g = torch.Generator().manual_seed(12)
+        ids = torch.randint(0, cfg.vocab_size, (2, t), generator=g)
+        tgt = torch.randint(0, cfg.vocab_size, (2, t), generator=g)
+        inner_mask = (torch.rand(2, t, generator=g) < 0.7).to(torch.float64)
+        outer_mask = 1.0 - inner_mask
+        inner, outer = meta_mod.meta_step(model, ids, tgt, inner_mask, outer_mask, inner_lr=lr, inner_steps=steps,
+                                          param_filter=pfilter, chunk_size=chunk)
+        outer.backward()
+        rec.update({f"{name}/w/{n}": p_.detach().numpy() for n, p_ in model.state_dict().items()})
+        rec.update({f"{name}/g/{n}": p_.grad.numpy() for n, p_ in model.named_parameters() if p_.grad is not None})
+        rec.update({f"{name}/ids": ids.numpy(), f"{name}/tgt": tgt.numpy(), f"{name}/inner_mask": inner_mask.numpy(),
+                    f"{name}/outer_mask": outer_mask.numpy(),
+                    f"{name}/losses": np.array([inner.item(), outer.item()])})
+    np.savez_compressed(out_path, **rec)
+    print(f"wrote {out_path.name}")
+
+
 def main() -> None:
     ttt_e2e_window_cases(HERE / "ttt_e2e_windows_fp64.npz")
+    ttt_e2e_meta_cases(HERE / "ttt_e2e_meta_fp64.npz")
     ta = load_reference()
     importlib.import_module("ref_ttt_kernels.backward_stubs")
     from_p_function_backwards(HERE / "from_p_function_backwards_t48_d16_fp64.npz")
