@@ -62,6 +62,13 @@ CONFIGS = {
     "c2pc": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=True, scale_in=0.5, step="from_p", flush=True,
                  workload="BASELINE config 2: fwd (P written) + first-order backward from P "
                           "(dv/rowsum/dq+dk from P) b=2 h=4 T=2048 d=128 fp16 causal"),
+    # forward only (the reference's tests/bench.py: triton_attention forward at config 2's shape)
+    "c2f": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5, step="fwd", flush=True,
+                workload="forward only, BASELINE config 2 shape: b=2 h=4 T=2048 d=128 fp16 non-causal"),
+    "c2fc": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=True, scale_in=0.5, step="fwd", flush=True,
+                 workload="forward only, BASELINE config 2 shape: b=2 h=4 T=2048 d=128 fp16 causal"),
+    "c4f": dict(b=8, h=32, t=16384, d=128, dtype="bf16", causal=True, scale_in=0.5, step="fwd",
+                workload="forward only, BASELINE config 4 shape: b=8 h=32 T=16384 d=128 bf16 causal"),
     # the TTT-E2E meta step (one inner SGD step with create_graph, outer loss backward)
     "c5": dict(b=1, h=12, t=8192, d=64, dtype="bf16", causal=True, scale_in=1.0, step="meta",
                model=dict(n_layers=12, d_model=768, n_heads=12, d_ff=3072, vocab_size=32000, max_seq_len=8192,
@@ -88,7 +95,7 @@ def causal_factor(t: int, causal: bool) -> float:
 def step_flops(cfg: dict, heads: int) -> float:
     """Algorithmic flops of one step: 28 T^2 d per head for the grad-grad step,
     12 T^2 d for forward + first-order backward (the from-P step)."""
-    units = 12.0 if cfg.get("step") == "from_p" else 28.0
+    units = {"from_p": 12.0, "fwd": 4.0}.get(cfg.get("step"), 28.0)
     return units * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
 
 
@@ -180,6 +187,57 @@ def make_inputs(cfg: dict, heads: range, device: torch.device, seed: int = 1234)
     return head_inputs(heads, cfg["t"], cfg["d"], dtype, device, seed=seed, scale_in=cfg["scale_in"])
 
 
+def math_path_step(kind: str):
+    """The reference's math formulation on the GPU (torch matmul / masked_fill /
+    softmax, triton_attention.py:18-25) in the same dtype, differentiated by
+    autograd as the reference's recompute path does (:416-420): the baseline the
+    north-star speed-up is quoted against. Materializes [t, t] tensors."""
+    from testtimeideas_b200.attention import attention_math
+
+    def step(x: dict, causal: bool):
+        scale = 1.0 / math.sqrt(x["q"].shape[-1])
+        if kind == "fwd":
+            with torch.no_grad():
+                return (attention_math(x["q"], x["k"], x["v"], causal, scale),)
+        q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+        o = attention_math(q, k, v, causal, scale)
+        dq, dk, dv = torch.autograd.grad(o, (q, k, v), x["do"], create_graph=True)
+        return torch.autograd.grad((dq, dk, dv), (q, k, v), (x["uq"], x["uk"], x["uv"]))
+    return step
+
+
+def time_math_path(cfg: dict, x: dict, kind: str, steps: int, device) -> Optional[dict]:
+    """CUDA-event time of the math path on the same inputs, when its [t, t]
+    intermediates fit comfortably (about 12 of them per head in flight)."""
+    heads = x["q"].shape[0] * x["q"].shape[1]
+    if kind not in ("gradgrad", "fwd") or heads * cfg["t"] ** 2 * 2 * 12 > 48 * 2 ** 30:
+        return None
+    step = math_path_step(kind)
+    try:
+        for _ in range(2):
+            step(x, cfg["causal"])
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step(x, cfg["causal"])
+        e1.record()
+        torch.cuda.synchronize(device)
+    except torch.cuda.OutOfMemoryError:
+        return {"unavailable": "out of memory"}
+    finally:
+        torch.cuda.empty_cache()
+    return {"ms_per_step": e0.elapsed_time(e1) / steps,
+            "what": "the reference's math formulation (torch matmul/softmax, autograd) on this GPU, same inputs"}
+
+
+def fwd_step(x: dict, causal: bool):
+    """Forward only, through the public API without a graph (inference)."""
+    from ttt_kernels import triton_attention
+    with torch.no_grad():
+        return (triton_attention(x["q"], x["k"], x["v"], causal=causal),)
+
+
 def from_p_step(x: dict, causal: bool):
     """Forward writing P, then the first-order backward from P through the
     reference-compatible backward_stubs helpers (the data flow of the reference's
@@ -263,10 +321,11 @@ def verify_sharded(cfg: dict, results, total_heads: int, device: torch.device) -
 
 
 def step_fn(cfg: dict):
-    return from_p_step if cfg.get("step") == "from_p" else gradgrad_step
+    return {"from_p": from_p_step, "fwd": fwd_step}.get(cfg.get("step"), gradgrad_step)
 
 
-STEP_INPUTS = {"gradgrad": ("q", "k", "v", "do", "uq", "uk", "uv"), "from_p": ("q", "k", "v", "do")}
+STEP_INPUTS = {"gradgrad": ("q", "k", "v", "do", "uq", "uk", "uv"), "from_p": ("q", "k", "v", "do"),
+               "fwd": ("q", "k", "v")}
 
 
 def run_meta(args, cfg: dict) -> None:
@@ -420,7 +479,7 @@ def run_ours(args, cfg: dict) -> None:
     host_in = {n: torch.empty_like(t, device="cpu").pin_memory() for n, t in x.items()}
     for n, t in x.items():
         host_in[n].copy_(t)
-    host_out = [torch.empty_like(x["q"], device="cpu").pin_memory() for _ in range(3)]
+    host_out = [torch.empty_like(x["q"], device="cpu").pin_memory() for _ in range(1 if kind == "fwd" else 3)]
     dev_in = {n: torch.empty_like(t) for n, t in x.items()}
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out)
@@ -475,6 +534,12 @@ def run_ours(args, cfg: dict) -> None:
         barrier()
     del last
 
+    math_path = None
+    if world == 1 and not args.no_math_path:
+        math_path = time_math_path(cfg, x, kind, args.steps, device)
+        if math_path and "ms_per_step" in math_path:
+            math_path["ours_speedup"] = math_path["ms_per_step"] / ms_per_step
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, args.cpu_t, reps=1)
@@ -502,6 +567,8 @@ def run_ours(args, cfg: dict) -> None:
         }
         if verify is not None:
             line["verify"] = verify
+        if math_path is not None:
+            line["math_path_gpu"] = math_path
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -518,6 +585,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-t", type=int, default=4096, help="T of the one-head CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-math-path", action="store_true",
+                    help="skip timing the reference's math formulation on the GPU beside the kernels")
     ap.add_argument("--verify", action="store_true",
                     help="gather the last step's grad-grads to rank 0 and check them against rank 0 running "
                          "every head alone (untimed)")
