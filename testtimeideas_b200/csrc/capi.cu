@@ -225,6 +225,76 @@ class ProfScope {
   cudaEvent_t start_ = nullptr;
 };
 
+// ---------------------------------------------------------------- side stream
+// The two passes that follow each other's inputs but not each other's outputs
+// (dK/dV and dQ of the backward; dd_q and dd_k/dd_v of the double backward)
+// run on the caller's stream and on a library-owned side stream that forks
+// from it and joins back (event record / wait only, no host synchronization),
+// so that one pass's last CTAs overlap the other's first, when the passes
+// are small (overlap_pays). While profiling is on, everything stays on the
+// caller's stream so that each launch's events time that kernel alone.
+struct Side {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mu;
+std::map<int, Side> g_side;
+
+// Overlap pays when a pass has too few CTAs to fill the GPU for long (under two
+// waves of one CTA per SM); with more, the passes' tails are short and running
+// them side by side only mixes their working sets in L2.
+bool overlap_pays(const ttt_problem& pb) {
+  static int sms = [] {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return 0;
+    return n;
+  }();
+  const int64_t ctas = static_cast<int64_t>(pb.b) * pb.h * ((pb.t + 127) / 128);
+  return sms > 0 && ctas < 2 * static_cast<int64_t>(sms);
+}
+
+class Fork {
+ public:
+  Fork(cudaStream_t main, bool enable) : main_(main), side_(main) {
+    if (!enable) return;
+    {
+      std::lock_guard<std::mutex> lk(g_prof_mu);
+      if (g_prof_on) return;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    std::lock_guard<std::mutex> lk(g_side_mu);
+    Side& sd = g_side[dev];
+    if (sd.stream == nullptr) {
+      if (cudaStreamCreateWithFlags(&sd.stream, cudaStreamNonBlocking) != cudaSuccess) {
+        sd.stream = nullptr;
+        return;
+      }
+      if (cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&sd.join, cudaEventDisableTiming) != cudaSuccess)
+        return;
+    }
+    if (sd.fork == nullptr || sd.join == nullptr) return;
+    if (cudaEventRecord(sd.fork, main_) != cudaSuccess || cudaStreamWaitEvent(sd.stream, sd.fork, 0) != cudaSuccess)
+      return;
+    side_ = sd.stream;
+    join_ = sd.join;
+  }
+  // The stream for the second pass (the caller's stream when not forked).
+  cudaStream_t side() const { return side_; }
+  ~Fork() {
+    if (side_ == main_ || join_ == nullptr) return;
+    std::lock_guard<std::mutex> lk(g_side_mu);
+    cudaEventRecord(join_, side_);
+    cudaStreamWaitEvent(main_, join_, 0);
+  }
+
+ private:
+  cudaStream_t main_, side_;
+  cudaEvent_t join_ = nullptr;
+};
+
 }  // namespace
 
 extern "C" {
@@ -310,6 +380,7 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     TTT_TRY(launched(ttt::launch_delta(da, s)));
   }
 
+  Fork fork(s, overlap_pays(pb));
   // dK, dV: key-major.
   {
     KParams k;
@@ -342,8 +413,9 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     k.lse2 = a->lse2;
     k.delta = a->delta;
     set_out0(k, a->dq);
-    ProfScope prof(TTT_K_BWD_Q, s);
-    TTT_TRY(launched(ttt::launch_qm(k, pb.d, bf16, causal, ttt::kBwdQ, false, s)));
+    cudaStream_t s2 = fork.side();
+    ProfScope prof(TTT_K_BWD_Q, s2);
+    TTT_TRY(launched(ttt::launch_qm(k, pb.d, bf16, causal, ttt::kBwdQ, false, s2)));
   }
   return TTT_OK;
 }
@@ -398,9 +470,11 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   kq.out_f1 = nullptr;
   set_out0(kq, a->gq);
   if (gdo) set_out1(kq, a->gdout);
+  Fork fork(s, overlap_pays(pb));
   {
-    ProfScope prof(TTT_K_BWD2_Q, s);
-    TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s)));
+    cudaStream_t s2 = fork.side();
+    ProfScope prof(TTT_K_BWD2_Q, s2);
+    TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s2)));
   }
 
   // Key-major: dd_k, dd_v.
