@@ -150,6 +150,9 @@ class ClockSampler:
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+        # nvidia-smi's start-up (NVML initialization) can stall CUDA API calls of this
+        # process for milliseconds: let it settle before a timed region begins
+        time.sleep(0.5)
 
     def stop(self) -> dict:
         if self.proc is None:
