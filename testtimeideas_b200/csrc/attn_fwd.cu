@@ -305,6 +305,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 //                             O0 += P0_n V_n, S0_{n+1}, O1 += P1_n V_n, S1_{n+1}.
 //                             While one warpgroup exponentiates tile n the
 //                             tensor core works on the other query tile.
+//   warps 10,11 idle (they complete the control warpgroup for the register split).
 //   warps 0..3  softmax of Q0, warps 4..7 softmax of Q1 (thread = query row =
 //                             TMEM lane): reads S_n, keeps the running max and
 //                             sum, writes 16-bit P_n back over the first 64
@@ -332,12 +333,21 @@ struct Fwd2Cfg {
   static constexpr int B_Q = 0, B_K = 1, B_V = 1 + NSTAGE, B_E = 1 + 2 * NSTAGE, B_S = 1 + 3 * NSTAGE;
   static constexpr int B_P = B_S + 2, B_O = B_P + 2, B_DR = B_O + 2, NBAR = B_DR + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-  static constexpr int NTHREADS = 320;
+  // Three warpgroups: two softmax warpgroups and a control warpgroup (MMA
+  // issuer, TMA producer, two idle warps). The launch gives every thread
+  // REG_LAUNCH registers (three warps share one 16K-register sub-partition);
+  // the control warpgroup then drops to REG_CTRL and the softmax warpgroups,
+  // which hold a full 128-column score row each, rise to REG_SOFTMAX.
+  static constexpr int NTHREADS = 384;
+  static constexpr int REG_LAUNCH = 168;
+  static constexpr int REG_CTRL = D == 64 ? 56 : 72;  // the d=128 MMA loop needs more than 56
+  static constexpr int REG_SOFTMAX = (3 * REG_LAUNCH - REG_CTRL) / 2;
+  static_assert(2 * REG_SOFTMAX + REG_CTRL <= 3 * REG_LAUNCH, "register split exceeds the launch allocation");
   static_assert(SMEM <= 232448, "two-tile forward exceeds shared memory");
 };
 
 template <int D, bool BF16, bool CAUSAL>
-__global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant__ KParams p) {
+__global__ void __launch_bounds__(384, 1) attn_fwd2_kernel(const __grid_constant__ KParams p) {
   using C = Fwd2Cfg<D>;
   constexpr int BM = C::BM, BN = C::BN, NP = D / 64, NS = C::NSTAGE;
   extern __shared__ uint8_t smem_raw[];
@@ -397,7 +407,9 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
   const uint32_t tmem = *tmem_slot;
   Guard g{abort_flag, p.err};
 
-  if (warp == 9) {
+  if (warp >= 8) {
+   regs_release<C::REG_CTRL>();
+   if (warp == 9) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch(&p.own[0]);
@@ -427,7 +439,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
         mbar_drain(v_full + j % NS, (j / NS) & 1);
       }
     }
-  } else if (warp == 8) {
+   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(128, BN, BF16, false, false);
@@ -481,8 +493,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd2_kernel(const __grid_constant
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
+   }
   } else {
     // ------------------------------------------------------------ softmax warps 0..7
+    regs_claim<C::REG_SOFTMAX>();
     const int w = warp >> 2, quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int row = q0 + w * BM + r;
@@ -592,6 +606,13 @@ template <int D, bool BF16, bool CAUSAL>
 static cudaError_t launch_fwd2_t(const KParams& p, cudaStream_t stream) {
   using C = Fwd2Cfg<D>;
   auto kern = attn_fwd2_kernel<D, BF16, CAUSAL>;
+  // The register split may only hand out what the launch allocated; a build
+  // whose register count came out lower is refused rather than launched.
+  static const int launch_regs = [&] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kern) == cudaSuccess ? a.numRegs : 0;
+  }();
+  if (launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, (p.T + 2 * C::BM - 1) / (2 * C::BM));

@@ -226,6 +226,24 @@ TTT_DEV void tmem_st16_raw(uint32_t taddr, const uint32_t (&w)[16]) {
 }
 TTT_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---------------------------------------------------------------- register split
+// Per-warpgroup register budget (setmaxnreg). Every warp of a warpgroup must
+// execute the same one. The increases draw on registers released by the
+// decreases out of the block's launch allocation (threads x registers at
+// launch), so the new budgets, summed over the block's warpgroups, must not
+// exceed that allocation; the host checks the sum against the kernel's
+// register count before launching.
+template <int N>
+TTT_DEV void regs_release() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg takes a multiple of 8 in [24, 256]");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+template <int N>
+TTT_DEV void regs_claim() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg takes a multiple of 8 in [24, 256]");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor, 128-byte swizzle (the layout TMA writes for
 // a box whose inner extent is 128 bytes). Fields: start address >> 4 [0,14),
