@@ -20,7 +20,10 @@ Reported (one JSON line from rank 0):
   roofline  the dominant kernel's algorithmic TFLOP/s against the measured bf16 peak;
   cpu_baseline  the reference's math path (oracle port, fp32, host cores) on a bounded sample.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4|c3|c3nc|c2]
+Workloads whose inputs are smaller than twice the L2 size (config 3, config 2)
+are timed with an L2 flush between steps, outside the per-step events.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4|c3|c3s|c3nc|c2|...]
 """
 
 from __future__ import annotations
@@ -50,6 +53,14 @@ CONFIGS = {
                workload="BASELINE config 3 (largest T): grad-grad b=1 h=1 T=16384 d=64 fp16 causal"),
     "c3nc": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=False, scale_in=1.0,
                  workload="BASELINE config 3 (largest T): grad-grad b=1 h=1 T=16384 d=64 fp16 non-causal"),
+    # config 3 in the loss form of the reference's own sweep (tests/bench_gradgrad_sweep.py:56-61):
+    # loss = mean(O), grads with create_graph, s = sum of mean(g^2), grad-grads of s
+    "c3s": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=True, scale_in=1.0, step="sweep",
+                workload="BASELINE config 3 (largest T), the reference sweep's loss form: loss = mean(O), "
+                         "s = sum mean(g^2), b=1 h=1 T=16384 d=64 fp16 causal"),
+    "c3snc": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=False, scale_in=1.0, step="sweep",
+                  workload="BASELINE config 3 (largest T), the reference sweep's loss form: loss = mean(O), "
+                           "s = sum mean(g^2), b=1 h=1 T=16384 d=64 fp16 non-causal"),
     "c4x8": dict(b=1, h=8, t=16384, d=128, dtype="bf16", causal=True, scale_in=0.5,
                  workload="8-head slice of BASELINE config 4 (profiling size): T=16384 d=128 bf16 causal"),
     "c2": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5,
@@ -204,33 +215,42 @@ def math_path_step(kind: str):
                 return (attention_math(x["q"], x["k"], x["v"], causal, scale),)
         q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
         o = attention_math(q, k, v, causal, scale)
+        if kind == "sweep":
+            grads = torch.autograd.grad(o.float().mean(), (q, k, v), create_graph=True)
+            return torch.autograd.grad(sum(g.float().pow(2).mean() for g in grads), (q, k, v))
         dq, dk, dv = torch.autograd.grad(o, (q, k, v), x["do"], create_graph=True)
         return torch.autograd.grad((dq, dk, dv), (q, k, v), (x["uq"], x["uk"], x["uv"]))
     return step
 
 
-def time_math_path(cfg: dict, x: dict, kind: str, steps: int, device) -> Optional[dict]:
+def time_math_path(cfg: dict, x: dict, kind: str, steps: int, device,
+                   flush: Optional[torch.Tensor] = None) -> Optional[dict]:
     """CUDA-event time of the math path on the same inputs, when its [t, t]
-    intermediates fit comfortably (about 12 of them per head in flight)."""
+    intermediates fit comfortably (about 12 of them per head in flight); with
+    `flush`, L2 is flushed between steps outside the per-step events, as for ours."""
     heads = x["q"].shape[0] * x["q"].shape[1]
-    if kind not in ("gradgrad", "fwd") or heads * cfg["t"] ** 2 * 2 * 12 > 48 * 2 ** 30:
+    if kind not in ("gradgrad", "fwd", "sweep") or heads * cfg["t"] ** 2 * 2 * 12 > 48 * 2 ** 30:
         return None
     step = math_path_step(kind)
     try:
         for _ in range(2):
             step(x, cfg["causal"])
         torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        evs = []
         for _ in range(steps):
+            if flush is not None:
+                flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
             step(x, cfg["causal"])
-        e1.record()
+            e1.record()
+            evs.append((e0, e1))
         torch.cuda.synchronize(device)
     except torch.cuda.OutOfMemoryError:
         return {"unavailable": "out of memory"}
     finally:
         torch.cuda.empty_cache()
-    return {"ms_per_step": e0.elapsed_time(e1) / steps,
+    return {"ms_per_step": sum(a.elapsed_time(b) for a, b in evs) / steps,
             "what": "the reference's math formulation (torch matmul/softmax, autograd) on this GPU, same inputs"}
 
 
@@ -254,6 +274,17 @@ def from_p_step(x: dict, causal: bool):
     rs = bs.triton_attn_rowsum_from_p(p, do, v, causal=causal)
     dq, dk = bs.triton_attn_bwd_dqdk_from_p(q, k, v, do, p, rs, causal=causal, scale=scale)
     return dq, dk, dv
+
+
+def sweep_step(x: dict, causal: bool):
+    """One step in the loss form of the reference's sweep (tests/bench_gradgrad_sweep.py:56-61):
+    loss = mean(O); grads with create_graph; s = sum over q, k, v of mean(g^2); grad-grads of s.
+    The upstream gradient of O is a constant and the probes are 2 g / numel."""
+    from ttt_kernels import triton_attention
+    q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+    o = triton_attention(q, k, v, causal=causal)
+    grads = torch.autograd.grad(o.float().mean(), (q, k, v), create_graph=True)
+    return torch.autograd.grad(sum(g.float().pow(2).mean() for g in grads), (q, k, v))
 
 
 def gradgrad_step(x: dict, causal: bool):
@@ -324,11 +355,14 @@ def verify_sharded(cfg: dict, results, total_heads: int, device: torch.device) -
 
 
 def step_fn(cfg: dict):
-    return {"from_p": from_p_step, "fwd": fwd_step}.get(cfg.get("step"), gradgrad_step)
+    return {"from_p": from_p_step, "fwd": fwd_step, "sweep": sweep_step}.get(cfg.get("step"), gradgrad_step)
 
 
 STEP_INPUTS = {"gradgrad": ("q", "k", "v", "do", "uq", "uk", "uv"), "from_p": ("q", "k", "v", "do"),
-               "fwd": ("q", "k", "v")}
+               "fwd": ("q", "k", "v"), "sweep": ("q", "k", "v")}
+# L2 of one B200; workloads whose inputs are smaller than twice this are timed with
+# an L2 flush between steps
+L2_BYTES = 126 << 20
 
 
 def run_meta(args, cfg: dict) -> None:
@@ -439,9 +473,11 @@ def run_ours(args, cfg: dict) -> None:
     for _ in range(args.warmup):
         step(x, cfg["causal"])
     _lib.check_device_errors(device)
-    # Workloads that fit in L2 get an L2 flush (a 512 MiB write) between timed
-    # steps, outside the per-step events; the others are larger than L2.
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device) if cfg.get("flush") else None
+    # Workloads whose inputs are not well above L2 get an L2 flush (a 512 MiB write)
+    # between timed steps, outside the per-step events; the others are larger than L2.
+    in_bytes = sum(t.numel() * t.element_size() for t in x.values())
+    need_flush = cfg.get("flush") or in_bytes < 2 * L2_BYTES
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device) if need_flush else None
 
     # ---- device-timed region: inputs resident in HBM. Timed without the profiling
     # hook (with it on, the library keeps every launch on one stream so that each
@@ -547,7 +583,7 @@ def run_ours(args, cfg: dict) -> None:
 
     math_path = None
     if world == 1 and not args.no_math_path:
-        math_path = time_math_path(cfg, x, kind, args.steps, device)
+        math_path = time_math_path(cfg, x, kind, args.steps, device, flush)
         if math_path and "ms_per_step" in math_path:
             math_path["ours_speedup"] = math_path["ms_per_step"] / ms_per_step
 
@@ -564,7 +600,8 @@ def run_ours(args, cfg: dict) -> None:
             "config": {"workload": cfg["workload"], "b": cfg["b"], "h": cfg["h"], "t": cfg["t"], "d": cfg["d"],
                        "causal": cfg["causal"], "global_heads": total_heads, "heads_per_gpu": heads,
                        "parallelism": f"bh-shard x{world}",
-                       "l2": ("L2 flushed (512 MiB write) between timed steps" if flush is not None else
+                       "l2": ("L2 flushed (512 MiB write) between timed steps (inputs %.1f MiB per GPU)" % (
+                                  in_bytes / 2 ** 20) if flush is not None else
                               "inputs larger than L2 (%d tensors of %.2f GiB per GPU%s)" % (
                                   len(x), x["q"].numel() * x["q"].element_size() / 2 ** 30,
                                   ", plus P" if kind == "from_p" else ""))},
