@@ -16,6 +16,14 @@
  *  - Row statistics (lse2, delta, gamma, rho) are fp32 arrays [b*h, t_pad]
  *    with t_pad = ttt_attn_t_pad(t) = roundup(t, 128), owned by the caller.
  *  - Nothing here allocates device memory; all buffers come from the caller.
+ *  - Optional work space (`work`, `work_bytes` in the pass arguments): a
+ *    caller-owned device buffer of at least ttt_attn_work_bytes(pb) bytes,
+ *    256-byte aligned, lets a pass whose grid is too small to fill the GPU
+ *    (few heads, causal) split each CTA's stream of tiles over several CTAs
+ *    and sum their fp32 partial results in a fixed order afterwards. With
+ *    work == NULL or too small a buffer the pass runs unsplit. The two forms
+ *    compute the same quantities; their fp32 summation orders differ, so the
+ *    16-bit results may differ in the last bit.
  *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
  *    stream); no entry point synchronizes the host.
  *  - Return value: TTT_OK or a ttt_status code. Argument errors are detected
@@ -35,7 +43,7 @@
 extern "C" {
 #endif
 
-#define TTT_ATTN_ABI_VERSION 2
+#define TTT_ATTN_ABI_VERSION 3
 
 enum ttt_status {
   TTT_OK = 0,
@@ -89,6 +97,8 @@ typedef struct {
   float* lse2;
   void* p;
   int32_t* err;
+  void* work; /* optional work space (see the conventions above) */
+  int64_t work_bytes;
 } ttt_fwd_args;
 int ttt_attn_fwd(const ttt_fwd_args* a, void* stream);
 
@@ -105,6 +115,8 @@ typedef struct {
   float* delta;
   ttt_view dq, dk, dv;
   int32_t* err;
+  void* work; /* optional work space (see the conventions above) */
+  int64_t work_bytes;
 } ttt_bwd_args;
 int ttt_attn_bwd(const ttt_bwd_args* a, void* stream);
 
@@ -127,6 +139,8 @@ typedef struct {
   ttt_view gq, gk, gv;
   ttt_view gdout;
   int32_t* err;
+  void* work; /* optional work space (see the conventions above) */
+  int64_t work_bytes;
 } ttt_bwd2_args;
 int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream);
 
@@ -183,8 +197,9 @@ int ttt_attn_profile_enable(int on);
 int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds);
 
 /* Allocation-free double backward (no counterpart in the reference). Same
- * arguments and results as ttt_attn_bwd2, except that a->gamma and a->rho are
- * ignored: the two scratch rows come from a fixed array built into the library
+ * arguments and results as ttt_attn_bwd2, except that a->gamma, a->rho and
+ * a->work are ignored (the passes run unsplit): the two scratch rows come from
+ * a fixed array built into the library
  * (2 * TTT_ATTN_NOALLOC_MAX_ROWS floats, 8 MiB, held by every GPU that loads
  * the library until the process exits), so callers that may not allocate
  * device memory during execution supply only inputs and outputs. Requires
@@ -198,6 +213,13 @@ int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream);
 
 /* roundup(t, 128): the row count of every statistics array. */
 int ttt_attn_t_pad(int t);
+/* Bytes of work space with which every pass of problem *pb (forward,
+ * backward, double backward with or without the dout gradient) can split its
+ * work; 0 when none of them would split (enough CTAs to fill the GPU, or a
+ * non-causal or banded problem, whose CTAs are of equal length). Depends on
+ * the current device's SM count. No reference counterpart (the reference's
+ * Triton launches pick their grid per call). */
+int64_t ttt_attn_work_bytes(const ttt_problem* pb);
 /* Static description of a status code. */
 const char* ttt_attn_status_string(int status);
 /* TTT_ATTN_ABI_VERSION of the loaded library. */

@@ -21,7 +21,7 @@ HEADER = ROOT / "include" / "ttt_attn.h"
 
 def _declared_functions():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(ttt_attn_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int64_t|int|const char\*)\s+(ttt_attn_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -45,10 +45,22 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_host_helpers(lib):
-    assert lib.ttt_attn_abi_version() == 2
+    assert lib.ttt_attn_abi_version() == 3
     assert lib.ttt_attn_t_pad(1) == 128 and lib.ttt_attn_t_pad(128) == 128 and lib.ttt_attn_t_pad(129) == 256
     assert lib.ttt_attn_status_string(0) == b"ok"
     assert b"64 or 128" in lib.ttt_attn_status_string(3)
+
+
+def test_work_bytes_query(lib):
+    # invalid problems need no work space; without a GPU the SM count is unknown, so nothing splits
+    bad = _lib.Problem(1, 1, 128, 96, 0, 1, 0.125)
+    assert lib.ttt_attn_work_bytes(ctypes.byref(bad)) == 0
+    assert lib.ttt_attn_work_bytes(None) == 0
+    noncausal = _lib.Problem(1, 1, 16384, 64, 0, 0, 0.125)
+    assert lib.ttt_attn_work_bytes(ctypes.byref(noncausal)) == 0
+    if not torch.cuda.is_available():
+        causal = _lib.Problem(1, 1, 16384, 64, 0, 1, 0.125)
+        assert lib.ttt_attn_work_bytes(ctypes.byref(causal)) == 0
 
 
 def _fwd_args(**over):

@@ -37,13 +37,15 @@ class Problem(ctypes.Structure):
 
 class FwdArgs(ctypes.Structure):
     _fields_ = [("pb", Problem), ("q", View), ("k", View), ("v", View), ("o", View),
-                ("lse2", ctypes.c_void_p), ("p", ctypes.c_void_p), ("err", ctypes.c_void_p)]
+                ("lse2", ctypes.c_void_p), ("p", ctypes.c_void_p), ("err", ctypes.c_void_p),
+                ("work", ctypes.c_void_p), ("work_bytes", ctypes.c_int64)]
 
 
 class BwdArgs(ctypes.Structure):
     _fields_ = [("pb", Problem), ("q", View), ("k", View), ("v", View), ("o", View), ("dout", View),
                 ("lse2", ctypes.c_void_p), ("delta", ctypes.c_void_p),
-                ("dq", View), ("dk", View), ("dv", View), ("err", ctypes.c_void_p)]
+                ("dq", View), ("dk", View), ("dv", View), ("err", ctypes.c_void_p),
+                ("work", ctypes.c_void_p), ("work_bytes", ctypes.c_int64)]
 
 
 class Bwd2Args(ctypes.Structure):
@@ -51,7 +53,8 @@ class Bwd2Args(ctypes.Structure):
                 ("lse2", ctypes.c_void_p), ("delta", ctypes.c_void_p),
                 ("uq", View), ("uk", View), ("uv", View),
                 ("gamma", ctypes.c_void_p), ("rho", ctypes.c_void_p),
-                ("gq", View), ("gk", View), ("gv", View), ("gdout", View), ("err", ctypes.c_void_p)]
+                ("gq", View), ("gk", View), ("gv", View), ("gdout", View), ("err", ctypes.c_void_p),
+                ("work", ctypes.c_void_p), ("work_bytes", ctypes.c_int64)]
 
 
 class FromPArgs(ctypes.Structure):
@@ -63,7 +66,8 @@ class FromPArgs(ctypes.Structure):
 # Every symbol include/ttt_attn.h declares.
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
             "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect",
-            "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p", "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p")
+            "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p", "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p",
+            "ttt_attn_work_bytes")
 NOALLOC_MAX_ROWS = 1 << 20  # TTT_ATTN_NOALLOC_MAX_ROWS
 KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv", "from_p")
 
@@ -91,6 +95,8 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         lib.ttt_attn_status_string.restype = ctypes.c_char_p
         lib.ttt_attn_status_string.argtypes = [ctypes.c_int]
         lib.ttt_attn_abi_version.restype = ctypes.c_int
+        lib.ttt_attn_work_bytes.restype = ctypes.c_int64
+        lib.ttt_attn_work_bytes.argtypes = [ctypes.c_void_p]
         lib.ttt_attn_selftest_umma.restype = ctypes.c_int
         lib.ttt_attn_selftest_umma.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -200,6 +206,17 @@ def validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
         raise ValueError("q, k, v must be on one device")
 
 
+def work_space(pb: Problem, device: torch.device):
+    """(buffer, pointer, bytes) of the work space with which the passes of `pb`
+    split their tiles over more CTAs (include/ttt_attn.h); (None, None, 0) when
+    no pass would split. The caching allocator's blocks are 512-byte aligned."""
+    n = int(load_library().ttt_attn_work_bytes(ctypes.byref(pb)))
+    if n <= 0:
+        return None, None, 0
+    buf = torch.empty(n, dtype=torch.uint8, device=device)
+    return buf, buf.data_ptr(), n
+
+
 def _stream() -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -220,8 +237,10 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: 
         lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         # causal: the kernel writes only key tiles up to the diagonal; the rest stays zero
         p = (torch.zeros if causal else torch.empty)((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
-        args = FwdArgs(problem(q, causal, scale, window), view(q), view(k), view(v), view(o), lse2.data_ptr(),
-                       p.data_ptr() if p is not None else None, error_word(q.device).data_ptr())
+        pb = problem(q, causal, scale, window)
+        work, wptr, wbytes = work_space(pb, q.device)
+        args = FwdArgs(pb, view(q), view(k), view(v), view(o), lse2.data_ptr(),
+                       p.data_ptr() if p is not None else None, error_word(q.device).data_ptr(), wptr, wbytes)
         _check(lib.ttt_attn_fwd(ctypes.byref(args), _stream()))
         if _SYNC_CHECK:
             check_device_errors(q.device)
@@ -237,9 +256,11 @@ def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0
     with torch.cuda.device(q.device):
         dq, dk, dv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
         delta = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
-        args = BwdArgs(problem(q, causal, scale, window), view(q), view(k), view(v), view(o), view(dout),
+        pb = problem(q, causal, scale, window)
+        work, wptr, wbytes = work_space(pb, q.device)
+        args = BwdArgs(pb, view(q), view(k), view(v), view(o), view(dout),
                        lse2.data_ptr(), delta.data_ptr(), view(dq), view(dk), view(dv),
-                       error_word(q.device).data_ptr())
+                       error_word(q.device).data_ptr(), wptr, wbytes)
         _check(lib.ttt_attn_bwd(ctypes.byref(args), _stream()))
         if _SYNC_CHECK:
             check_device_errors(q.device)
@@ -269,9 +290,11 @@ def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float
         gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
         gamma = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         rho = torch.empty_like(gamma)
-        args = Bwd2Args(problem(q, causal, scale, window), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
+        pb = problem(q, causal, scale, window)
+        work, wptr, wbytes = work_space(pb, q.device)
+        args = Bwd2Args(pb, view(q), view(k), view(v), view(dout), lse2.data_ptr(),
                         delta.data_ptr(), view(uq), view(uk), view(uv), gamma.data_ptr(), rho.data_ptr(),
-                        view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr())
+                        view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr(), wptr, wbytes)
         _check(lib.ttt_attn_bwd2(ctypes.byref(args), _stream()))
         if _SYNC_CHECK:
             check_device_errors(q.device)

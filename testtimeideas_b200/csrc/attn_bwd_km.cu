@@ -12,9 +12,10 @@
 //             reference approximates with torch.matmul in
 //             backward_stubs.py:435-514)
 //
-// Roles (320 threads): warps 0..7 elementwise (warp w: TMEM lanes
+// Roles (384 threads): warps 0..7 elementwise (warp w: TMEM lanes
 // 32*(w%4)..+31, tile columns (w/4)*32..+32), warp 8 MMA issuer, warp 9 TMA
-// producer. The per-query statistics (lse2, delta, gamma, rho) of each tile
+// producer, warps 10-11 idle (they complete the control warpgroup, which
+// gives registers to the elementwise warpgroups with setmaxnreg). The per-query statistics (lse2, delta, gamma, rho) of each tile
 // arrive with it through TMA and are read with broadcast 16-byte loads.
 //
 // The elementwise results E (16-bit P^T, dS^T | dS^T, G_S^T, G_dP^T) live in
@@ -60,7 +61,12 @@ struct KmCfg {
   static constexpr int NA = 2;
   static constexpr int NCW = 8;
   static constexpr int NCT = NCW * 32;
-  static constexpr int NTHREADS = NCT + 64;
+  static constexpr int NTHREADS = NCT + 128;  // + the control warpgroup
+  // Register split: the launch gives every thread REG_LAUNCH registers (three
+  // warps share one 16K-register sub-partition); the control warpgroup then
+  // drops to REG_CTRL and the two elementwise warpgroups rise to REG_ELEM.
+  static constexpr int REG_LAUNCH = 168, REG_CTRL = 152, REG_ELEM = (3 * REG_LAUNCH - REG_CTRL) / 2;
+  static_assert(REG_ELEM % 8 == 0 && 2 * REG_ELEM + REG_CTRL <= 3 * REG_LAUNCH, "register split");
   static constexpr int CPW = BM / 2;
   static constexpr int TILE_R = BK * D * 2;
   // streamed: ST0 = [Q; u_q] (or Q), ST1 = dO
@@ -150,7 +156,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // split mode: this CTA takes share `share` of its key block's query tiles
+  const int nsplit = p.nsplit > 1 ? p.nsplit : 1;
+  const int bh = blockIdx.x / nsplit, share = blockIdx.x % nsplit;
   const int bidx = bh / p.H, hidx = bh % p.H;
   const int kblk = blockIdx.y;  // causal: small kblk has the most query tiles, launched first
   const int k0 = kblk * BK;
@@ -159,9 +167,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   // Causal: this key block meets query tiles from its diagonal up to the last
   // query that sees its last key.
   const Band band = Band::make(p, CAUSAL);
-  const int qt0 = CAUSAL ? (k0 / BM) : 0;
+  const int qt_first = CAUSAL ? (k0 / BM) : 0;
   const int qt_end = CAUSAL ? min(n_q, band.last_query(min(k0 + BK, T) - 1) / BM + 1) : n_q;
-  const int n_tiles = qt_end - qt0;
+  const int qt0 = qt_first + split_begin(qt_end - qt_first, share, nsplit);
+  const int n_tiles = qt_first + split_begin(qt_end - qt_first, share + 1, nsplit) - qt0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
@@ -198,7 +207,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     return tmem + off;
   };
 
-  if (warp == WARP_LOAD) {
+  if (warp >= C::NCW) {
+   regs_release<C::REG_CTRL>();
+   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       for (int t = 0; t < C::NR; ++t) tma_prefetch(&p.own[t]);
@@ -229,7 +240,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-  } else if (warp == WARP_MMA) {
+   } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_n1 = idesc_f16(128, BM, BF16, false, false);
@@ -356,8 +367,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
+   }
   } else {
     // ------------------------------------------------------------ elementwise warps 0..7
+    regs_claim<C::REG_ELEM>();
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const int key = k0 + r;
@@ -472,13 +485,20 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     }
     if (ok && mbar_wait(acc_full, 0, g, 8)) {
       tc_fence_after();
-      const bool valid = key < T;
-      uint16_t* r0 = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
-                     static_cast<int64_t>(key) * p.o0_st;
-      uint16_t* r1 = p.out1 + static_cast<int64_t>(bidx) * p.o1_sb + static_cast<int64_t>(hidx) * p.o1_sh +
-                     static_cast<int64_t>(key) * p.o1_st;
-      acc_cols_to_global<D / 2, BF16>(tAcc0 + lane_off, half * (D / 2), r0, valid, scale);
-      acc_cols_to_global<D / 2, BF16>(tAcc1 + lane_off, half * (D / 2), r1, valid, 1.f);
+      if (nsplit > 1) {
+        // unscaled fp32 partials of this share (rows up to t_pad exist in the work space)
+        const int64_t row = (static_cast<int64_t>(share) * p.B * p.H + bh) * p.t_pad + key;
+        acc_cols_to_f32<D / 2>(tAcc0 + lane_off, half * (D / 2), p.part0 + row * D, n_tiles > 0);
+        acc_cols_to_f32<D / 2>(tAcc1 + lane_off, half * (D / 2), p.part1 + row * D, n_tiles > 0);
+      } else {
+        const bool valid = key < T;
+        uint16_t* r0 = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
+                       static_cast<int64_t>(key) * p.o0_st;
+        uint16_t* r1 = p.out1 + static_cast<int64_t>(bidx) * p.o1_sb + static_cast<int64_t>(hidx) * p.o1_sh +
+                       static_cast<int64_t>(key) * p.o1_st;
+        acc_cols_to_global<D / 2, BF16>(tAcc0 + lane_off, half * (D / 2), r0, valid, scale);
+        acc_cols_to_global<D / 2, BF16>(tAcc1 + lane_off, half * (D / 2), r1, valid, 1.f);
+      }
     }
   }
 
@@ -492,9 +512,16 @@ template <int D, bool BF16, bool CAUSAL, int KIND>
 static cudaError_t launch_km_t(const KParams& p, cudaStream_t stream) {
   using C = KmCfg<D, KIND>;
   auto kern = attn_km_kernel<D, BF16, CAUSAL, KIND>;
+  // The register split may only hand out what the launch allocated; a build
+  // whose register count came out lower is refused rather than launched.
+  static const int launch_regs = [&] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kern) == cudaSuccess ? a.numRegs : 0;
+  }();
+  if (launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.B * p.H, (p.T + C::BK - 1) / C::BK);
+  dim3 grid(p.B * p.H * (p.nsplit > 1 ? p.nsplit : 1), (p.T + C::BK - 1) / C::BK);
   kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }

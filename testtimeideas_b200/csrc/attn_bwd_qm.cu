@@ -15,8 +15,10 @@
 //            double backward of TritonDvFn / TritonRowSumFn / TritonDqDkFn,
 //            backward_stubs.py:435-514, with the complete second-order terms)
 //
-// Roles (320 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
-// thread), warp 9 TMA producer. Compute warp w owns TMEM lanes 32*(w%4)..+31
+// Roles (384 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
+// thread), warp 9 TMA producer, warps 10-11 idle (they complete the control
+// warpgroup, which gives registers to the elementwise warpgroups with
+// setmaxnreg). Compute warp w owns TMEM lanes 32*(w%4)..+31
 // (one query row per thread) and columns (w/4)*BN/2 .. +BN/2 of every tile.
 //
 // Score products that share their A operand run as one N = 2*BN product: the
@@ -49,7 +51,12 @@ struct QmCfg {
   static constexpr int NA = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 2 : 1));
   static constexpr int NCW = 8;
   static constexpr int NCT = NCW * 32;
-  static constexpr int NTHREADS = NCT + 64;
+  static constexpr int NTHREADS = NCT + 128;  // + the control warpgroup
+  // Register split: the launch gives every thread REG_LAUNCH registers (three
+  // warps share one 16K-register sub-partition); the control warpgroup then
+  // drops to REG_CTRL and the two elementwise warpgroups rise to REG_ELEM.
+  static constexpr int REG_LAUNCH = 168, REG_CTRL = 152, REG_ELEM = (3 * REG_LAUNCH - REG_CTRL) / 2;
+  static_assert(REG_ELEM % 8 == 0 && 2 * REG_ELEM + REG_CTRL <= 3 * REG_LAUNCH, "register split");
   static constexpr int CPW = BN / 2;
   // streamed tiles: ST0 = [K; u_k] (or K), ST1 = [V; u_v] (or V), rows stacked per panel
   static constexpr int ST_ROWS = BWD2 ? 2 * BN : BN;
@@ -132,7 +139,9 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   auto tileE = [&](int s, int t) { return C::EIS ? tileS(s, 1) + t * C::TILE_E : sE + t * C::TILE_E; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // split mode: this CTA takes share `share` of its query block's key tiles
+  const int nsplit = p.nsplit > 1 ? p.nsplit : 1;
+  const int bh = blockIdx.x / nsplit, share = blockIdx.x % nsplit;
   const int bidx = bh / p.H, hidx = bh % p.H;
   const int qblk = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.y;
   const int q0 = qblk * BM;
@@ -140,8 +149,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const int n_all = (T + BN - 1) / BN;
   // Causal: key tiles before the first row's band, or past the diagonal, are skipped.
   const Band band = Band::make(p, CAUSAL);
-  const int n_first = CAUSAL ? band.lo(q0) / BN : 0;  // first key tile visited
-  const int n_tiles = (CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all) - n_first;
+  const int n_lo = CAUSAL ? band.lo(q0) / BN : 0;  // first key tile the block visits
+  const int n_hi = CAUSAL ? min(n_all, (q0 + BM - 1) / BN + 1) : n_all;
+  const int n_first = n_lo + split_begin(n_hi - n_lo, share, nsplit);  // first key tile of this share
+  const int n_tiles = n_lo + split_begin(n_hi - n_lo, share + 1, nsplit) - n_first;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
@@ -172,7 +183,9 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const uint32_t tUQ = tDO + (C::RT_DO ? D / 2 : 0);
   Guard g{abort_flag, p.err};
 
-  if (warp == WARP_LOAD) {
+  if (warp >= C::NCW) {
+   regs_release<C::REG_CTRL>();
+   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       constexpr int NSTR = C::BWD2 ? 4 : 2;
@@ -201,7 +214,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-  } else if (warp == WARP_MMA) {
+   } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_n1 = idesc_f16(128, BN, BF16, false, false);
@@ -336,8 +349,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
+   }
   } else {
     // ------------------------------------------------------------ elementwise warps 0..7
+    regs_claim<C::REG_ELEM>();
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const int row = q0 + r;
@@ -480,7 +495,13 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         red[r * 4 + 3] = a4;
       }
       compute_bar<C::NCT>();
-      if (half == 0 && ok && !*abort_flag) {
+      if (half == 0 && ok && !*abort_flag && nsplit > 1) {
+        // this share's four row sums; the reduction forms gamma and rho from their totals
+        const float4 sums = make_float4(a_g + red[r * 4 + 0], a2 + red[r * 4 + 1], a3 + red[r * 4 + 2],
+                                        a4 + red[r * 4 + 3]);
+        reinterpret_cast<float4*>(p.part0)[(static_cast<int64_t>(share) * p.B * p.H + bh) * p.t_pad + row] =
+            valid ? sums : make_float4(0.f, 0.f, 0.f, 0.f);
+      } else if (half == 0 && ok && !*abort_flag) {
         a_g += red[r * 4 + 0];
         a2 += red[r * 4 + 1];
         a3 += red[r * 4 + 2];
@@ -492,13 +513,21 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     } else {
       if (ok && mbar_wait(acc_full, 0, g, 8)) {
         tc_fence_after();
-        uint16_t* r0 = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
-                       static_cast<int64_t>(row) * p.o0_st;
-        acc_cols_to_global<D / 2, BF16>(tAcc0 + lane_off, half * (D / 2), r0, valid, scale);
-        if constexpr (KIND == kBwd2Q && GDO) {
-          uint16_t* r1 = p.out1 + static_cast<int64_t>(bidx) * p.o1_sb + static_cast<int64_t>(hidx) * p.o1_sh +
-                         static_cast<int64_t>(row) * p.o1_st;
-          acc_cols_to_global<D / 2, BF16>(tAcc1 + lane_off, half * (D / 2), r1, valid, 1.f);
+        if (nsplit > 1) {
+          // unscaled fp32 partials of this share (rows up to t_pad exist in the work space)
+          const int64_t prow = (static_cast<int64_t>(share) * p.B * p.H + bh) * p.t_pad + row;
+          acc_cols_to_f32<D / 2>(tAcc0 + lane_off, half * (D / 2), p.part0 + prow * D, n_tiles > 0);
+          if constexpr (KIND == kBwd2Q && GDO)
+            acc_cols_to_f32<D / 2>(tAcc1 + lane_off, half * (D / 2), p.part1 + prow * D, n_tiles > 0);
+        } else {
+          uint16_t* r0 = p.out0 + static_cast<int64_t>(bidx) * p.o0_sb + static_cast<int64_t>(hidx) * p.o0_sh +
+                         static_cast<int64_t>(row) * p.o0_st;
+          acc_cols_to_global<D / 2, BF16>(tAcc0 + lane_off, half * (D / 2), r0, valid, scale);
+          if constexpr (KIND == kBwd2Q && GDO) {
+            uint16_t* r1 = p.out1 + static_cast<int64_t>(bidx) * p.o1_sb + static_cast<int64_t>(hidx) * p.o1_sh +
+                           static_cast<int64_t>(row) * p.o1_st;
+            acc_cols_to_global<D / 2, BF16>(tAcc1 + lane_off, half * (D / 2), r1, valid, 1.f);
+          }
         }
       }
     }
@@ -514,9 +543,16 @@ template <int D, bool BF16, bool CAUSAL, int KIND, bool GDO>
 static cudaError_t launch_qm_t(const KParams& p, cudaStream_t stream) {
   using C = QmCfg<D, KIND, GDO>;
   auto kern = attn_qm_kernel<D, BF16, CAUSAL, KIND, GDO>;
+  // The register split may only hand out what the launch allocated; a build
+  // whose register count came out lower is refused rather than launched.
+  static const int launch_regs = [&] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kern) == cudaSuccess ? a.numRegs : 0;
+  }();
+  if (launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.B * p.H, (p.T + C::BM - 1) / C::BM);
+  dim3 grid(p.B * p.H * (p.nsplit > 1 ? p.nsplit : 1), (p.T + C::BM - 1) / C::BM);
   kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }

@@ -55,7 +55,19 @@ struct KParams {
   float scale;       // softmax scale applied to Q K^T
   float scale_log2;  // scale * log2(e)
   int* err;          // device error word (0 = ok), may be null
+  // Split mode (nsplit > 1; passes that support it): grid column x works on head
+  // x / nsplit and on share x % nsplit of its block's tile stream, and writes
+  // unscaled fp32 partial results part0 / part1, [nsplit][b*h][t_pad][d], in place
+  // of out0 / out1; a reduction kernel sums the shares in order afterwards.
+  int nsplit;
+  float* part0;
+  float* part1;
 };
+
+// Contiguous share `split` of `n` items cut into `nsplit` nearly equal parts.
+TTT_DEV int split_begin(int n, int split, int nsplit) {
+  return static_cast<int>((static_cast<int64_t>(n) * split) / nsplit);
+}
 
 // Causal attention with a lower bound on each row's visible keys: key j is
 // visible to query i iff lo(i) <= j <= i. Kinds:

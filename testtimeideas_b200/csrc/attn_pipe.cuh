@@ -162,4 +162,24 @@ TTT_DEV void acc_cols_to_global(uint32_t taddr_row, int col0, uint16_t* dst_row,
   }
 }
 
+// Split mode: copy NCOLS fp32 accumulator columns col0.. of this thread's TMEM
+// lane to an fp32 partial row (zeros when `have` is false: a share without
+// tiles never wrote its accumulator). Warp-collective like the loads.
+template <int NCOLS>
+TTT_DEV void acc_cols_to_f32(uint32_t taddr_row, int col0, float* dst_row, bool have) {
+#pragma unroll
+  for (int c = 0; c < NCOLS / 32; ++c) {
+    float v[32];
+    if (have) {
+      tmem_ld32(taddr_row + col0 + c * 32, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+    float4* d4 = reinterpret_cast<float4*>(dst_row + col0 + c * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+}
+
 }  // namespace ttt

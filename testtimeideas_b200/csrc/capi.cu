@@ -243,15 +243,96 @@ std::map<int, Side> g_side;
 // Overlap pays when a pass has too few CTAs to fill the GPU for long (under two
 // waves of one CTA per SM); with more, the passes' tails are short and running
 // them side by side only mixes their working sets in L2.
-bool overlap_pays(const ttt_problem& pb) {
+int sm_count() {
   static int sms = [] {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return 0;
     return n;
   }();
+  return sms;
+}
+
+bool overlap_pays(const ttt_problem& pb) {
+  const int sms = sm_count();
   const int64_t ctas = static_cast<int64_t>(pb.b) * pb.h * ((pb.t + 127) / 128);
   return sms > 0 && ctas < 2 * static_cast<int64_t>(sms);
+}
+
+// ---------------------------------------------------------------- split planning
+// A causal pass over few heads has few CTAs of very unequal length (the first
+// key block of a head meets every query tile, the last one a single tile), so
+// the longest CTA sets the pass's time while most SMs idle. Such a pass splits
+// each CTA's tile stream into `nsplit` nearly equal shares, one CTA each, so
+// that the grid holds about 1.5 CTAs per SM; the shares' fp32 partials are
+// summed in order by a reduction kernel. Non-causal and banded problems have
+// CTAs of equal length and stay unsplit.
+int split_count(const ttt_problem& pb) {
+  const int sms = sm_count();
+  if (pb.causal == 0 || pb.window > 0 || sms <= 0) return 1;
+  const int64_t base = static_cast<int64_t>(pb.b) * pb.h * ((pb.t + 127) / 128);
+  if (2 * base >= 3 * static_cast<int64_t>(sms)) return 1;
+  const int64_t n = (3 * static_cast<int64_t>(sms) + 2 * base - 1) / (2 * base);
+  return static_cast<int>(n < 2 ? 2 : (n > 4 ? 4 : n));
+}
+
+// The work space of a split problem: four slices of [nsplit][b*h][t_pad][d]
+// fp32. The key-major passes write their two partial arrays into slices 0 and
+// 1, the query-major passes (which may run at the same time on the side
+// stream) into 2 and 3; the row-statistics pass (float4 per row) uses slice 0
+// before the key-major pass runs.
+constexpr int kWorkSlices = 4;
+int64_t slice_floats(const ttt_problem& pb, int nsplit) {
+  return static_cast<int64_t>(nsplit) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * pb.d;
+}
+int64_t work_need(const ttt_problem& pb) {
+  const int n = split_count(pb);
+  return n > 1 ? kWorkSlices * slice_floats(pb, n) * 4 : 0;
+}
+
+struct Work {
+  int nsplit = 1;  // 1: run unsplit
+  float* base = nullptr;
+  int64_t slice = 0;
+  float* at(int i) const { return base + i * slice; }
+};
+Work plan_work(const ttt_problem& pb, void* work, int64_t work_bytes) {
+  Work w;
+  const int n = split_count(pb);
+  if (n <= 1 || work == nullptr || work_bytes < work_need(pb) || (reinterpret_cast<uintptr_t>(work) & 255u) != 0)
+    return w;
+  w.nsplit = n;
+  w.base = static_cast<float*>(work);
+  w.slice = slice_floats(pb, n);
+  return w;
+}
+void use_work(KParams& k, const Work& w, int first_slice) {
+  k.nsplit = w.nsplit;
+  if (w.nsplit > 1) {
+    k.part0 = w.at(first_slice);
+    k.part1 = w.at(first_slice + 1);
+  }
+}
+
+// Sums the shares of n_out (1 or 2) partial arrays starting at slice
+// first_slice into out0 (times scale0) and out1 (times scale1).
+int reduce_splits(const Work& w, int first_slice, const ttt_problem& pb, int n_out, const ttt_view& out0,
+                  float scale0, const ttt_view* out1, float scale1, cudaStream_t s) {
+  ttt::SplitReduceArgs r;
+  std::memset(&r, 0, sizeof(r));
+  const ttt_view* outs[2] = {&out0, out1};
+  const float scales[2] = {scale0, scale1};
+  for (int i = 0; i < n_out; ++i) {
+    r.part[i] = w.at(first_slice + i);
+    r.out[i] = static_cast<uint16_t*>(outs[i]->ptr);
+    r.sb[i] = outs[i]->sb, r.sh[i] = outs[i]->sh, r.st[i] = outs[i]->st;
+    r.scale[i] = scales[i];
+  }
+  r.n_out = n_out;
+  r.nsplit = w.nsplit;
+  r.B = pb.b, r.H = pb.h, r.T = pb.t, r.t_pad = ttt_attn_t_pad(pb.t), r.D = pb.d;
+  r.bf16 = pb.dtype == TTT_BF16;
+  return launched(ttt::launch_split_reduce(r, s));
 }
 
 class Fork {
@@ -302,6 +383,11 @@ extern "C" {
 int ttt_attn_t_pad(int t) { return (t + 127) / 128 * 128; }
 
 int ttt_attn_abi_version(void) { return TTT_ATTN_ABI_VERSION; }
+
+int64_t ttt_attn_work_bytes(const ttt_problem* pb) {
+  if (pb == nullptr || check_problem(*pb) != TTT_OK) return 0;
+  return work_need(*pb);
+}
 
 const char* ttt_attn_status_string(int s) {
   switch (s) {
@@ -380,6 +466,7 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     TTT_TRY(launched(ttt::launch_delta(da, s)));
   }
 
+  const Work w = plan_work(pb, a->work, a->work_bytes);
   Fork fork(s, overlap_pays(pb));
   // dK, dV: key-major.
   {
@@ -395,8 +482,10 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad, rows));
     set_out0(k, a->dk);
     set_out1(k, a->dv);
+    use_work(k, w, 0);
     ProfScope prof(TTT_K_BWD_KV, s);
     TTT_TRY(launched(ttt::launch_km(k, pb.d, bf16, causal, ttt::kBwdKV, s)));
+    if (w.nsplit > 1) TTT_TRY(reduce_splits(w, 0, pb, 2, a->dk, pb.scale, &a->dv, 1.f, s));
   }
   // dQ: query-major.
   {
@@ -413,9 +502,11 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
     k.lse2 = a->lse2;
     k.delta = a->delta;
     set_out0(k, a->dq);
+    use_work(k, w, 2);
     cudaStream_t s2 = fork.side();
     ProfScope prof(TTT_K_BWD_Q, s2);
     TTT_TRY(launched(ttt::launch_qm(k, pb.d, bf16, causal, ttt::kBwdQ, false, s2)));
+    if (w.nsplit > 1) TTT_TRY(reduce_splits(w, 2, pb, 1, a->dq, pb.scale, nullptr, 0.f, s2));
   }
   return TTT_OK;
 }
@@ -458,9 +549,23 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   kq.delta = a->delta;
   kq.out_f0 = a->gamma;
   kq.out_f1 = a->rho;
+  const Work w = plan_work(pb, a->work, a->work_bytes);
   {
+    use_work(kq, w, 0);
     ProfScope prof(TTT_K_BWD2_STATS, s);
     TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kStats, false, s)));
+    if (w.nsplit > 1) {
+      ttt::StatsReduceArgs r;
+      r.part = reinterpret_cast<const float4*>(w.at(0));
+      r.delta = a->delta;
+      r.gamma = a->gamma;
+      r.rho = a->rho;
+      r.nsplit = w.nsplit;
+      r.BH = bh;
+      r.T = pb.t;
+      r.t_pad = t_pad;
+      TTT_TRY(launched(ttt::launch_stats_reduce(r, s)));
+    }
   }
   if (ttt::qm_tile_cols(pb.d, ttt::kBwd2Q, gdo) != ttt::qm_tile_cols(pb.d, ttt::kStats, false))
     TTT_TRY(encode_stream_q(ttt::qm_tile_cols(pb.d, ttt::kBwd2Q, gdo)));
@@ -470,11 +575,13 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   kq.out_f1 = nullptr;
   set_out0(kq, a->gq);
   if (gdo) set_out1(kq, a->gdout);
+  use_work(kq, w, 2);
   Fork fork(s, overlap_pays(pb));
   {
     cudaStream_t s2 = fork.side();
     ProfScope prof(TTT_K_BWD2_Q, s2);
     TTT_TRY(launched(ttt::launch_qm(kq, pb.d, bf16, causal, ttt::kBwd2Q, gdo, s2)));
+    if (w.nsplit > 1) TTT_TRY(reduce_splits(w, 2, pb, gdo ? 2 : 1, a->gq, pb.scale, &a->gdout, 1.f, s2));
   }
 
   // Key-major: dd_k, dd_v.
@@ -496,8 +603,10 @@ int ttt_attn_bwd2(const ttt_bwd2_args* a, void* stream) {
   set_out0(kk, a->gk);
   set_out1(kk, a->gv);
   {
+    use_work(kk, w, 0);
     ProfScope prof(TTT_K_BWD2_KV, s);
     TTT_TRY(launched(ttt::launch_km(kk, pb.d, bf16, causal, ttt::kBwd2KV, s)));
+    if (w.nsplit > 1) TTT_TRY(reduce_splits(w, 0, pb, 2, a->gk, pb.scale, &a->gv, 1.f, s));
   }
   return TTT_OK;
 }

@@ -43,6 +43,31 @@ struct DeltaArgs {
 };
 cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream);
 
+// Split-mode reduction: out[b, h, t, :] = scale * sum over s (in order) of
+// part[s][b*h][t][:] for t < T, for up to two outputs (blockIdx.y).
+struct SplitReduceArgs {
+  const float* part[2];
+  uint16_t* out[2];
+  int64_t sb[2], sh[2], st[2];
+  float scale[2];
+  int n_out, nsplit;
+  int B, H, T, t_pad, D;
+  bool bf16;
+};
+cudaError_t launch_split_reduce(const SplitReduceArgs& a, cudaStream_t stream);
+
+// Split-mode reduction of the row statistics: part holds per share the four row
+// sums (sum P G_dS, sum P G_dS dP, sum P (dO u_v^T), sum P dP) as a float4 per
+// row, [nsplit][b*h][t_pad]; writes gamma and rho for rows t < T, 0 beyond.
+struct StatsReduceArgs {
+  const float4* part;
+  const float* delta;
+  float* gamma;
+  float* rho;
+  int nsplit, BH, T, t_pad;
+};
+cudaError_t launch_stats_reduce(const StatsReduceArgs& a, cudaStream_t stream);
+
 // Self-test GEMM used to validate descriptor conventions: C = A B with A a
 // 128 x K tile (K-major) and B either N x K (K-major, "score" form) or K x N
 // (MN-major, "accumulate" form); inputs through the same 4-D tensor maps.

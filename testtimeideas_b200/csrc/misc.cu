@@ -47,6 +47,75 @@ cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- split reduction
+// One thread per 8 consecutive columns of one output row: reads the row's 8
+// fp32 partials of every share (two 16-byte loads each, shares in order),
+// scales the sum and stores eight 16-bit values with one 16-byte store.
+template <bool BF16>
+__global__ void __launch_bounds__(256) split_reduce_kernel(SplitReduceArgs a) {
+  const int o = blockIdx.y;
+  const int per_row = a.D / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t bh_count = static_cast<int64_t>(a.B) * a.H;
+  if (idx >= bh_count * a.T * per_row) return;
+  const int c8 = static_cast<int>(idx % per_row);
+  const int64_t row = idx / per_row;
+  const int t = static_cast<int>(row % a.T);
+  const int bh = static_cast<int>(row / a.T);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < a.nsplit; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(
+        a.part[o] + ((static_cast<int64_t>(s) * bh_count + bh) * a.t_pad + t) * a.D + c8 * 8);
+    const float4 x = src[0], y = src[1];
+    acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
+    acc[4] += y.x; acc[5] += y.y; acc[6] += y.z; acc[7] += y.w;
+  }
+  const float m = a.scale[o];
+  uint4 w;
+  w.x = pack2<BF16>(acc[0] * m, acc[1] * m);
+  w.y = pack2<BF16>(acc[2] * m, acc[3] * m);
+  w.z = pack2<BF16>(acc[4] * m, acc[5] * m);
+  w.w = pack2<BF16>(acc[6] * m, acc[7] * m);
+  const int b = bh / a.H, h = bh % a.H;
+  *reinterpret_cast<uint4*>(a.out[o] + b * a.sb[o] + h * a.sh[o] + static_cast<int64_t>(t) * a.st[o] + c8 * 8) = w;
+}
+
+cudaError_t launch_split_reduce(const SplitReduceArgs& a, cudaStream_t stream) {
+  if (a.n_out < 1 || a.n_out > 2 || a.nsplit < 1 || (a.D % 8) != 0) return cudaErrorInvalidValue;
+  const int64_t n = static_cast<int64_t>(a.B) * a.H * a.T * (a.D / 8);
+  const dim3 grid(static_cast<unsigned>((n + 255) / 256), a.n_out);
+  if (a.bf16) split_reduce_kernel<true><<<grid, 256, 0, stream>>>(a);
+  else split_reduce_kernel<false><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+// gamma = sum of the shares' sum P G_dS; rho = A2 - delta gamma - gamma A4 + A3
+// from the summed A2 = sum P G_dS dP, A3 = sum P (dO u_v^T), A4 = sum P dP (the
+// identity the stats pass uses unsplit). One thread per row.
+__global__ void __launch_bounds__(256) stats_reduce_kernel(StatsReduceArgs a) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t rows = static_cast<int64_t>(a.BH) * a.t_pad;
+  if (row >= rows) return;
+  float g = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+  for (int s = 0; s < a.nsplit; ++s) {
+    const float4 v = a.part[static_cast<int64_t>(s) * rows + row];
+    g += v.x;
+    a2 += v.y;
+    a3 += v.z;
+    a4 += v.w;
+  }
+  const bool valid = static_cast<int>(row % a.t_pad) < a.T;
+  a.gamma[row] = valid ? g : 0.f;
+  a.rho[row] = valid ? a2 - a.delta[row] * g - g * a4 + a3 : 0.f;
+}
+
+cudaError_t launch_stats_reduce(const StatsReduceArgs& a, cudaStream_t stream) {
+  if (a.nsplit < 1) return cudaErrorInvalidValue;
+  const int64_t rows = static_cast<int64_t>(a.BH) * a.t_pad;
+  stats_reduce_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- self-test
 // C[128 x N] = A[128 x K] * B, B K-major ([N x K] rows) or MN-major ([K x N] rows).
 struct SelftestParams {

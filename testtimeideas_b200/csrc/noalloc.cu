@@ -69,5 +69,7 @@ extern "C" int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream) {
   ttt_bwd2_args args = *a;
   args.gamma = scratch;
   args.rho = scratch + kMaxRows;
+  args.work = nullptr;  // unsplit passes: no work space beyond the built-in rows
+  args.work_bytes = 0;
   return ttt_attn_bwd2(&args, stream);
 }
