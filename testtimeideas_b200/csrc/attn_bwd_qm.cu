@@ -15,10 +15,10 @@
 //            double backward of TritonDvFn / TritonRowSumFn / TritonDqDkFn,
 //            backward_stubs.py:435-514, with the complete second-order terms)
 //
-// Roles (384 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
-// thread), warp 9 TMA producer, warps 10-11 idle (they complete the control
-// warpgroup, which gives registers to the elementwise warpgroups with
-// setmaxnreg). Compute warp w owns TMEM lanes 32*(w%4)..+31
+// Roles (320 threads at d=128, 384 at d=64): warps 0..7 elementwise, warp 8
+// MMA issuer (one thread), warp 9 TMA producer; at d=64 warps 10-11 idle (they
+// complete the control warpgroup, which gives registers to the elementwise
+// warpgroups with setmaxnreg). Compute warp w owns TMEM lanes 32*(w%4)..+31
 // (one query row per thread) and columns (w/4)*BN/2 .. +BN/2 of every tile.
 //
 // Score products that share their A operand run as one N = 2*BN product: the
@@ -51,10 +51,13 @@ struct QmCfg {
   static constexpr int NA = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 2 : 1));
   static constexpr int NCW = 8;
   static constexpr int NCT = NCW * 32;
-  static constexpr int NTHREADS = NCT + 128;  // + the control warpgroup
-  // Register split: the launch gives every thread REG_LAUNCH registers (three
-  // warps share one 16K-register sub-partition); the control warpgroup then
-  // drops to REG_CTRL and the two elementwise warpgroups rise to REG_ELEM.
+  // Register split (d=64, whose elementwise code spills at the launch budget):
+  // the launch gives every thread REG_LAUNCH registers (three warps share one
+  // 16K-register sub-partition); the control warpgroup then drops to REG_CTRL
+  // and the two elementwise warpgroups rise to REG_ELEM. At d=128 the kernels
+  // fit the launch budget and run faster without the idle warps.
+  static constexpr bool SPLIT_REGS = D == 64;
+  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64);
   static constexpr int REG_LAUNCH = 168, REG_CTRL = 152, REG_ELEM = (3 * REG_LAUNCH - REG_CTRL) / 2;
   static_assert(REG_ELEM % 8 == 0 && 2 * REG_ELEM + REG_CTRL <= 3 * REG_LAUNCH, "register split");
   static constexpr int CPW = BN / 2;
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   Guard g{abort_flag, p.err};
 
   if (warp >= C::NCW) {
-   regs_release<C::REG_CTRL>();
+   if constexpr (C::SPLIT_REGS) regs_release<C::REG_CTRL>();
    if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -352,7 +355,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
    }
   } else {
     // ------------------------------------------------------------ elementwise warps 0..7
-    regs_claim<C::REG_ELEM>();
+    if constexpr (C::SPLIT_REGS) regs_claim<C::REG_ELEM>();
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const int row = q0 + r;
@@ -549,7 +552,7 @@ static cudaError_t launch_qm_t(const KParams& p, cudaStream_t stream) {
     cudaFuncAttributes a{};
     return cudaFuncGetAttributes(&a, kern) == cudaSuccess ? a.numRegs : 0;
   }();
-  if (launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
+  if (C::SPLIT_REGS && launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H * (p.nsplit > 1 ? p.nsplit : 1), (p.T + C::BM - 1) / C::BM);

@@ -368,7 +368,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd2_kernel(const __grid_constant
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // split mode: this CTA takes share `share` of its key-tile stream
+  const int nsplit = p.nsplit > 1 ? p.nsplit : 1;
+  const int bh = blockIdx.x / nsplit, share = blockIdx.x % nsplit;
   const int bidx = bh / p.H, hidx = bh % p.H;
   const int blk = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.y;  // longest rows first
   const int q0 = blk * 2 * BM;
@@ -379,14 +381,22 @@ __global__ void __launch_bounds__(384, 1) attn_fwd2_kernel(const __grid_constant
   // and past its diagonal are skipped.
   const Band band = Band::make(p, CAUSAL);
   const int qs0 = q0, qs1 = q0 + BM;
-  const int hi0 = qs0 >= T ? 0 : (CAUSAL ? min(n_all, qs0 / BN + 1) : n_all);
-  const int hi1 = qs1 >= T ? 0 : (CAUSAL ? min(n_all, qs1 / BN + 1) : n_all);
-  const int lo0 = CAUSAL ? band.lo(qs0) / BN : 0;
-  const int lo1 = CAUSAL ? band.lo(min(qs1, T - 1)) / BN : 0;
+  const int hi0_all = qs0 >= T ? 0 : (CAUSAL ? min(n_all, qs0 / BN + 1) : n_all);
+  const int hi1_all = qs1 >= T ? 0 : (CAUSAL ? min(n_all, qs1 / BN + 1) : n_all);
+  const int lo0_all = CAUSAL ? band.lo(qs0) / BN : 0;
+  const int lo1_all = CAUSAL ? band.lo(min(qs1, T - 1)) / BN : 0;
+  // the whole block streams key tiles [s_lo, s_hi); split mode gives this CTA
+  // a contiguous share of them (the two ranges overlap there: the split runs
+  // only without a band), and each query tile keeps its part of the share
+  const int s_lo = lo0_all;
+  const int s_hi = max(hi0_all, hi1_all > lo1_all ? hi1_all : 0);
+  const int a0 = s_lo + split_begin(s_hi - s_lo, share, nsplit), a1 = s_lo + split_begin(s_hi - s_lo, share + 1, nsplit);
+  const int lo0 = max(lo0_all, a0), hi0 = min(hi0_all, a1);
+  const int lo1 = max(lo1_all, a0), hi1 = min(hi1_all, a1);
   const int nt0 = max(0, hi0 - lo0), nt1 = max(0, hi1 - lo1);
   // the CTA streams key tiles n_lo .. n_lo + n_kv - 1 (relative index r = n - n_lo)
-  const int n_lo = lo0;
-  const int n_kv = max(hi0, nt1 > 0 ? hi1 : 0) - n_lo;
+  const int n_lo = nsplit > 1 ? a0 : lo0;
+  const int n_kv = nsplit > 1 ? a1 - a0 : max(hi0, nt1 > 0 ? hi1 : 0) - n_lo;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NBAR; ++i) mbar_init(bars + i, 1);
@@ -582,7 +592,16 @@ __global__ void __launch_bounds__(384, 1) attn_fwd2_kernel(const __grid_constant
       tc_fence_before();
       mbar_arrive(p_full + w);
     }
-    if (ok && ntw > 0) {
+    if (nsplit > 1) {
+      // unnormalized O row, running max (log2 domain) and sum of this share; a
+      // share without tiles for this query tile leaves (0, -inf, 0)
+      if (ok && (ntw == 0 || mbar_wait(pv_done + w, (ntw - 1) & 1, g, 9)) && row < p.t_pad) {
+        tc_fence_after();
+        const int64_t prow = (static_cast<int64_t>(share) * p.B * p.H + bh) * p.t_pad + row;
+        acc_cols_to_f32<D>(tO, 0, p.part0 + prow * D, ntw > 0);
+        reinterpret_cast<float2*>(p.part1)[prow] = ntw > 0 ? make_float2(m_used, l) : make_float2(-INFINITY, 0.f);
+      }
+    } else if (ok && ntw > 0) {
       if (mbar_wait(pv_done + w, (ntw - 1) & 1, g, 9)) {
         tc_fence_after();
         const bool valid = row < T;
@@ -615,7 +634,7 @@ static cudaError_t launch_fwd2_t(const KParams& p, cudaStream_t stream) {
   if (launch_regs < C::REG_LAUNCH) return cudaErrorLaunchOutOfResources;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.B * p.H, (p.T + 2 * C::BM - 1) / (2 * C::BM));
+  dim3 grid(p.B * p.H * (p.nsplit > 1 ? p.nsplit : 1), (p.T + 2 * C::BM - 1) / (2 * C::BM));
   kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }

@@ -267,10 +267,12 @@ bool overlap_pays(const ttt_problem& pb) {
 // that the grid holds about 1.5 CTAs per SM; the shares' fp32 partials are
 // summed in order by a reduction kernel. Non-causal and banded problems have
 // CTAs of equal length and stay unsplit.
-int split_count(const ttt_problem& pb) {
+// rows: the query rows (or keys) one unsplit CTA owns (128 in the backward
+// passes, 256 in the forward).
+int split_count(const ttt_problem& pb, int rows = 128) {
   const int sms = sm_count();
   if (pb.causal == 0 || pb.window > 0 || sms <= 0) return 1;
-  const int64_t base = static_cast<int64_t>(pb.b) * pb.h * ((pb.t + 127) / 128);
+  const int64_t base = static_cast<int64_t>(pb.b) * pb.h * ((pb.t + rows - 1) / rows);
   if (2 * base >= 3 * static_cast<int64_t>(sms)) return 1;
   const int64_t n = (3 * static_cast<int64_t>(sms) + 2 * base - 1) / (2 * base);
   return static_cast<int>(n < 2 ? 2 : (n > 4 ? 4 : n));
@@ -285,9 +287,17 @@ constexpr int kWorkSlices = 4;
 int64_t slice_floats(const ttt_problem& pb, int nsplit) {
   return static_cast<int64_t>(nsplit) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * pb.d;
 }
+// The forward's split uses [nsplit][b*h][t_pad][d] fp32 O rows followed by
+// [nsplit][b*h][t_pad] (max, sum) pairs.
+int64_t fwd_work_need(const ttt_problem& pb) {
+  const int n = split_count(pb, 256);
+  return n > 1 ? static_cast<int64_t>(n) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * (pb.d + 2) * 4 : 0;
+}
 int64_t work_need(const ttt_problem& pb) {
   const int n = split_count(pb);
-  return n > 1 ? kWorkSlices * slice_floats(pb, n) * 4 : 0;
+  const int64_t bwd = n > 1 ? kWorkSlices * slice_floats(pb, n) * 4 : 0;
+  const int64_t fwd = fwd_work_need(pb);
+  return bwd > fwd ? bwd : fwd;
 }
 
 struct Work {
@@ -428,9 +438,29 @@ int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
   set_out0(k, a->o);
   k.out_f0 = a->lse2;
   k.out1 = static_cast<uint16_t*>(a->p);
-  ProfScope prof(TTT_K_FWD, static_cast<cudaStream_t>(stream));
-  return launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr,
-                                  static_cast<cudaStream_t>(stream)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // split mode (the forward without P only): shares of each CTA's key stream
+  const int nf = a->p == nullptr ? split_count(pb, 256) : 1;
+  const bool split = nf > 1 && a->work != nullptr && a->work_bytes >= fwd_work_need(pb) &&
+                     (reinterpret_cast<uintptr_t>(a->work) & 255u) == 0;
+  const int64_t o_floats = static_cast<int64_t>(nf) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * pb.d;
+  if (split) {
+    k.nsplit = nf;
+    k.part0 = static_cast<float*>(a->work);
+    k.part1 = k.part0 + o_floats;
+  }
+  ProfScope prof(TTT_K_FWD, s);
+  TTT_TRY(launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr, s)));
+  if (!split) return TTT_OK;
+  ttt::FwdCombineArgs c;
+  c.part_o = k.part0;
+  c.part_ml = reinterpret_cast<const float2*>(k.part1);
+  c.out = static_cast<uint16_t*>(a->o.ptr);
+  c.sb = a->o.sb, c.sh = a->o.sh, c.st = a->o.st;
+  c.lse2 = a->lse2;
+  c.nsplit = nf, c.B = pb.b, c.H = pb.h, c.T = pb.t, c.t_pad = ttt_attn_t_pad(pb.t), c.D = pb.d;
+  c.bf16 = pb.dtype == TTT_BF16;
+  return launched(ttt::launch_fwd_combine(c, s));
 }
 
 int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {

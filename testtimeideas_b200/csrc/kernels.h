@@ -68,6 +68,22 @@ struct StatsReduceArgs {
 };
 cudaError_t launch_stats_reduce(const StatsReduceArgs& a, cudaStream_t stream);
 
+// Split-mode combination of the forward: per row and share, an unnormalized O
+// row (part_o, [nsplit][b*h][t_pad][d]) with its running max m (base-2 log
+// domain) and sum l (part_ml). Writes O = sum_s 2^(m_s - M) O_s / L and
+// lse2 = M + log2 L, M = max_s m_s, L = sum_s 2^(m_s - M) l_s; rows t >= T get
+// lse2 = +inf.
+struct FwdCombineArgs {
+  const float* part_o;
+  const float2* part_ml;
+  uint16_t* out;
+  int64_t sb, sh, st;
+  float* lse2;
+  int nsplit, B, H, T, t_pad, D;
+  bool bf16;
+};
+cudaError_t launch_fwd_combine(const FwdCombineArgs& a, cudaStream_t stream);
+
 // Self-test GEMM used to validate descriptor conventions: C = A B with A a
 // 128 x K tile (K-major) and B either N x K (K-major, "score" form) or K x N
 // (MN-major, "accumulate" form); inputs through the same 4-D tensor maps.

@@ -116,6 +116,54 @@ cudaError_t launch_stats_reduce(const StatsReduceArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// One thread per 8 columns of a row (the thread of column group 0 also writes lse2).
+template <bool BF16>
+__global__ void __launch_bounds__(256) fwd_combine_kernel(FwdCombineArgs a) {
+  const int per_row = a.D / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.t_pad;
+  if (idx >= rows * per_row) return;
+  const int c8 = static_cast<int>(idx % per_row);
+  const int64_t row = idx / per_row;  // bh * t_pad + t
+  const int t = static_cast<int>(row % a.t_pad);
+  if (t >= a.T) {
+    if (c8 == 0) a.lse2[row] = INFINITY;
+    return;
+  }
+  float M = -INFINITY;
+  for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, a.part_ml[static_cast<int64_t>(s) * rows + row].x);
+  float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < a.nsplit; ++s) {
+    const float2 ml = a.part_ml[static_cast<int64_t>(s) * rows + row];
+    if (ml.y == 0.f) continue;  // a share without keys for this row
+    const float w = exp2f(ml.x - M);
+    L += w * ml.y;
+    const float4* src = reinterpret_cast<const float4*>(a.part_o + (static_cast<int64_t>(s) * rows + row) * a.D + c8 * 8);
+    const float4 x = src[0], y = src[1];
+    o[0] += w * x.x; o[1] += w * x.y; o[2] += w * x.z; o[3] += w * x.w;
+    o[4] += w * y.x; o[5] += w * y.y; o[6] += w * y.z; o[7] += w * y.w;
+  }
+  const float inv = 1.f / L;
+  uint4 v;
+  v.x = pack2<BF16>(o[0] * inv, o[1] * inv);
+  v.y = pack2<BF16>(o[2] * inv, o[3] * inv);
+  v.z = pack2<BF16>(o[4] * inv, o[5] * inv);
+  v.w = pack2<BF16>(o[6] * inv, o[7] * inv);
+  const int bh = static_cast<int>(row / a.t_pad);
+  const int b = bh / a.H, h = bh % a.H;
+  *reinterpret_cast<uint4*>(a.out + b * a.sb + h * a.sh + static_cast<int64_t>(t) * a.st + c8 * 8) = v;
+  if (c8 == 0) a.lse2[row] = M + log2f(L);
+}
+
+cudaError_t launch_fwd_combine(const FwdCombineArgs& a, cudaStream_t stream) {
+  if (a.nsplit < 1 || (a.D % 8) != 0) return cudaErrorInvalidValue;
+  const int64_t n = static_cast<int64_t>(a.B) * a.H * a.t_pad * (a.D / 8);
+  const dim3 grid(static_cast<unsigned>((n + 255) / 256));
+  if (a.bf16) fwd_combine_kernel<true><<<grid, 256, 0, stream>>>(a);
+  else fwd_combine_kernel<false><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- self-test
 // C[128 x N] = A[128 x K] * B, B K-major ([N x K] rows) or MN-major ([K x N] rows).
 struct SelftestParams {
