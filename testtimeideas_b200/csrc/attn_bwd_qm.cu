@@ -15,8 +15,8 @@
 //            double backward of TritonDvFn / TritonRowSumFn / TritonDqDkFn,
 //            backward_stubs.py:435-514, with the complete second-order terms)
 //
-// Roles (320 threads at d=128, 384 at d=64): warps 0..7 elementwise, warp 8
-// MMA issuer (one thread), warp 9 TMA producer; at d=64 warps 10-11 idle (they
+// Roles (320 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
+// thread), warp 9 TMA producer (with SPLIT_REGS, 384 threads: warps 10-11 idle
 // complete the control warpgroup, which gives registers to the elementwise
 // warpgroups with setmaxnreg). Compute warp w owns TMEM lanes 32*(w%4)..+31
 // (one query row per thread) and columns (w/4)*BN/2 .. +BN/2 of every tile.
@@ -51,12 +51,12 @@ struct QmCfg {
   static constexpr int NA = KIND == kBwdQ ? 1 : (KIND == kStats ? 0 : (GDO ? 2 : 1));
   static constexpr int NCW = 8;
   static constexpr int NCT = NCW * 32;
-  // Register split (d=64, whose elementwise code spills at the launch budget):
-  // the launch gives every thread REG_LAUNCH registers (three warps share one
-  // 16K-register sub-partition); the control warpgroup then drops to REG_CTRL
-  // and the two elementwise warpgroups rise to REG_ELEM. At d=128 the kernels
-  // fit the launch budget and run faster without the idle warps.
-  static constexpr bool SPLIT_REGS = D == 64;
+  // Register split: the launch gives every thread REG_LAUNCH registers (three
+  // warps share one 16K-register sub-partition); the control warpgroup then
+  // drops to REG_CTRL and the two elementwise warpgroups rise to REG_ELEM. Off:
+  // it removes the small d=64 spills but the idle warps cost more (measured
+  // 0.8-1.2% slower per step).
+  static constexpr bool SPLIT_REGS = false;
   static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64);
   static constexpr int REG_LAUNCH = 168, REG_CTRL = 152, REG_ELEM = (3 * REG_LAUNCH - REG_CTRL) / 2;
   static_assert(REG_ELEM % 8 == 0 && 2 * REG_ELEM + REG_CTRL <= 3 * REG_LAUNCH, "register split");
