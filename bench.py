@@ -87,6 +87,15 @@ CONFIGS = {
                workload="BASELINE config 5: TTT-E2E meta step, 12 layers d_model=768 12 heads d_ff=3072 vocab 32000, "
                         "bf16, b=1 T=8192, inner_steps=1 inner_lr=0.01 on the first 6144 tokens, outer loss on the "
                         "last 2048, all parameters updated, attention on the kernels"),
+    # the forward-only streaming path of the reference's latency demo (scripts/demo_infer.py:11-27,
+    # :70-100): its model, seq 8192 in chunks of 512 new tokens, each call over the last 512 tokens
+    "c5s": dict(b=1, h=8, t=8192, d=64, dtype="bf16", causal=True, scale_in=1.0, step="stream",
+                window=512, chunk=512,
+                model=dict(n_layers=8, d_model=512, n_heads=8, d_ff=2048, vocab_size=4096, max_seq_len=10240,
+                           window_size=512, dropout=0.0),
+                workload="streaming inference of the reference's latency demo: 8 layers d_model=512 8 heads "
+                         "d_ff=2048 vocab 4096 window 512, bf16 (the demo's fp32 model cast: the kernels take "
+                         "16-bit), 8192 tokens in chunks of 512, each forward over the last 512 tokens"),
     "c8p": dict(b=1, h=8, t=8192, d=128, dtype="fp16", causal=False, scale_in=0.5, step="from_p",
                 workload="fwd (P written) + first-order backward from P, b=1 h=8 T=8192 d=128 fp16 "
                          "non-causal (P = 1 GiB, larger than L2)"),
@@ -436,6 +445,75 @@ def run_meta(args, cfg: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_stream(args, cfg: dict) -> None:
+    """Streaming inference (no graph): one timed step = the whole sequence streamed in
+    chunks (ttt_model.stream_logits); value = tokens per second."""
+    from testtimeideas_b200 import _lib, ttt_model
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("the streaming workload runs on one GPU")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    mcfg = ttt_model.ModelConfig(**cfg["model"])
+    torch.manual_seed(0)
+    model = ttt_model.TTTModel(mcfg).to(device, torch.bfloat16).eval()
+    t, window, chunk = cfg["t"], cfg["window"], cfg["chunk"]
+    g = torch.Generator(device=device).manual_seed(1)
+    tokens = torch.randint(0, mcfg.vocab_size, (1, t), generator=g, device=device)
+
+    def step(tok):
+        return ttt_model.stream_logits(model, tok, window, chunk)[-1]
+
+    clocks = ClockSampler(0)
+    for _ in range(args.warmup):
+        step(tokens)
+    _lib.check_device_errors(device)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(tokens)
+    e1.record()
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    _lib.profile_collect()
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        step(tokens)
+    torch.cuda.synchronize(device)
+    _lib.profile_enable(False)
+    prof = _lib.profile_collect()
+    # end to end: token ids from pinned host memory, the last chunk's logits back to the host
+    host = tokens.cpu().pin_memory()
+    dev = torch.empty_like(tokens)
+    last = step(tokens)
+    out_host = torch.empty(last.shape, dtype=last.dtype).pin_memory()
+    torch.cuda.synchronize(device)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        dev.copy_(host, non_blocking=True)
+        out_host.copy_(step(dev), non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    kern = {k: v for k, v in prof.items() if v[0] > 0}
+    attn_ms = sum(v[1] for v in kern.values()) / args.steps
+    line = {"metric": "TTT-E2E streaming inference tokens/s (forward-only path)", "value": t / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform token ids)",
+            "config": {"workload": cfg["workload"], "t": t, "window": window, "chunk": chunk,
+                       "l2": "weights and activations of 16 forward calls per step (not flushed)"},
+            "e2e": {"value": t / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": host.numel() * host.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+            "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms,
+            "kernel_ms_per_step": {k: v[1] / args.steps for k, v in kern.items()},
+            "gpu_launches": sum(v[0] for v in kern.values()), "clocks": clk, "roofline": None, "cpu_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, cfg: dict) -> None:
     from testtimeideas_b200 import _lib
     from testtimeideas_b200.sharding import head_range, max_over_ranks as _max_over_ranks
@@ -652,6 +730,8 @@ def main() -> None:
         run_reference(args, cfg)
     elif cfg.get("step") == "meta":
         run_meta(args, cfg)
+    elif cfg.get("step") == "stream":
+        run_stream(args, cfg)
     else:
         run_ours(args, cfg)
 

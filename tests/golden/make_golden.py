@@ -210,9 +210,49 @@ def ttt_e2e_meta_cases(out_path: Path) -> None:
     print(f"wrote {out_path.name}")
 
 
+# name, config overrides, t, inner_steps, inner_lr, param_filter, chunk_size, stream window/chunk
+INFER_CASES = [
+    ("infer_chunked", dict(window_size=8, suffix_layers=1), 24, 2, 0.05, "suffix_blocks,ln_f,head", 8, (8, 8)),
+    ("infer_full", dict(window_size=None, suffix_layers=-1), 16, 1, 0.1, None, None, (12, 4)),
+]
+
+
+def ttt_e2e_infer_cases(out_path: Path) -> None:
+    """Test-time adaptation at inference with the reference's ttt_apply and
+    ttt_logits (cloud_ttt_e2e/ttt_e2e/meta.py:180-224) on tiny float64 TTT models
+    on CPU, and streaming forwards as its latency demo runs them
+    (cloud_ttt_e2e/scripts/demo_infer.py:11-27): the adapted model's logits and
+    each streaming call's logits."""
+    load_reference_ttt_e2e()
+    model_mod, meta_mod = sys.modules["ref_ttt_e2e.model"], sys.modules["ref_ttt_e2e.meta"]
+    rec = {}
+    for name, over, t, steps, lr, pfilter, chunk, (window, schunk) in INFER_CASES:
+        cfg = model_mod.ModelConfig(vocab_size=64, max_seq_len=64, d_model=32, n_heads=2, n_layers=2, d_ff=64,
+                                    dropout=0.0, **over)
+        torch.manual_seed(21)
+        model = model_mod.TTTModel(cfg).double().eval()
+        g = torch.Generator().manual_seed(22)
+        ids = torch.randint(0, cfg.vocab_size, (1, t), generator=g)
+        tgt = torch.randint(0, cfg.vocab_size, (1, t), generator=g)
+        inner_mask = (torch.rand(1, t, generator=g) < 0.7).to(torch.float64)
+        params = meta_mod.ttt_apply(model, ids, tgt, inner_mask, inner_lr=lr, inner_steps=steps,
+                                    param_filter=pfilter, chunk_size=chunk)
+        with torch.no_grad():
+            logits = meta_mod.ttt_logits(model, params, ids, chunk_size=chunk)
+            stream = [model(ids[:, max(0, end - window):end])
+                      for end in (min(t, s0 + schunk) for s0 in range(0, t, schunk))]
+        rec.update({f"{name}/w/{n}": p_.detach().numpy() for n, p_ in model.state_dict().items()})
+        rec.update({f"{name}/ids": ids.numpy(), f"{name}/tgt": tgt.numpy(), f"{name}/inner_mask": inner_mask.numpy(),
+                    f"{name}/logits": logits.numpy()})
+        rec.update({f"{name}/stream{i}": x.numpy() for i, x in enumerate(stream)})
+    np.savez_compressed(out_path, **rec)
+    print(f"wrote {out_path.name}")
+
+
 def main() -> None:
     ttt_e2e_window_cases(HERE / "ttt_e2e_windows_fp64.npz")
     ttt_e2e_meta_cases(HERE / "ttt_e2e_meta_fp64.npz")
+    ttt_e2e_infer_cases(HERE / "ttt_e2e_infer_fp64.npz")
     ta = load_reference()
     importlib.import_module("ref_ttt_kernels.backward_stubs")
     from_p_function_backwards(HERE / "from_p_function_backwards_t48_d16_fp64.npz")

@@ -56,3 +56,45 @@ def test_meta_step_cuda_matches_cpu(window, suffix, chunk, pfilter):
         assert prof[kind][0] > 0, kind
     if pfilter is not None:
         assert prof["bwd2_q"][0] == 0
+
+
+def test_inference_adaptation_and_streaming_cuda_matches_cpu():
+    """ttt_apply + ttt_logits and streaming forwards (the forward-only path) on a bf16
+    CUDA model against float64 on CPU; the forward and first-order backward kernels run,
+    the double backward does not (no create_graph at inference)."""
+    cfg = ttt_model.ModelConfig(vocab_size=256, max_seq_len=512, d_model=128, n_heads=2, n_layers=2, d_ff=256,
+                                window_size=128, suffix_layers=1, dropout=0.0)
+    torch.manual_seed(5)
+    cpu = ttt_model.TTTModel(cfg).double().eval()
+    gpu = ttt_model.TTTModel(cfg).to("cuda", torch.bfloat16).eval()
+    gpu.load_state_dict({n: p.to(torch.bfloat16) for n, p in cpu.state_dict().items()})
+    t = 256
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(0, cfg.vocab_size, (1, t), generator=g)
+    tgt = torch.randint(0, cfg.vocab_size, (1, t), generator=g)
+    inner_mask = (torch.rand(1, t, generator=g) < 0.7).float()
+
+    def run(model, dev):
+        a = [x.to(dev) for x in (ids, tgt, inner_mask)]
+        params = ttt_model.ttt_apply(model, *a, inner_lr=0.05, inner_steps=2, param_filter="suffix_blocks,ln_f,head",
+                                     chunk_size=128)
+        with torch.no_grad():
+            logits = ttt_model.ttt_logits(model, params, a[0], chunk_size=128)
+        return logits, ttt_model.stream_logits(model, a[0], window_size=128, chunk_size=64)
+
+    ref_logits, ref_stream = run(cpu, "cpu")
+    _lib.profile_collect()
+    _lib.profile_enable(True)
+    logits, stream = run(gpu, "cuda")
+    torch.cuda.synchronize()
+    _lib.profile_enable(False)
+    prof = _lib.profile_collect()
+    _lib.check_device_errors()
+    rel = lambda x, r: float((x.double().cpu() - r).norm() / r.norm())  # noqa: E731
+    assert rel(logits, ref_logits) < 3e-2
+    assert len(stream) == len(ref_stream)
+    for x, r in zip(stream, ref_stream):
+        assert rel(x, r) < 3e-2
+    for kind in ("fwd", "bwd_kv", "bwd_q"):
+        assert prof[kind][0] > 0, kind
+    assert prof["bwd2_stats"][0] == 0

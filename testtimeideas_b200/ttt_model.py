@@ -152,32 +152,79 @@ def _chunks(x: torch.Tensor, size: Optional[int]) -> Sequence[torch.Tensor]:
     return x.split(size, dim=1)
 
 
+def _suffix_logits(model: TTTModel, params: Dict[str, torch.Tensor], hidden: torch.Tensor) -> torch.Tensor:
+    return functional_call(model, params, (None,), {"mode": "suffix", "prefix_hidden": hidden})
+
+
+def _inner_scan(model: TTTModel, params: Dict[str, torch.Tensor], fast: List[str], prefix: torch.Tensor, targets,
+                inner_mask, inner_lr: float, inner_steps: int, chunk_size: Optional[int],
+                create_graph: bool) -> Tuple[Dict[str, torch.Tensor], torch.Tensor]:
+    """``inner_steps`` SGD steps on each chunk's suffix loss, chunk after chunk, for
+    the parameters named in ``fast`` (cloud_ttt_e2e/ttt_e2e/meta.py:44-109); with
+    create_graph the updates stay differentiable (the meta step), without it they
+    are plain tensors (test-time adaptation at inference)."""
+    inner_losses = []
+    for hid, tgt, msk in zip(_chunks(prefix, chunk_size), _chunks(targets, chunk_size), _chunks(inner_mask, chunk_size)):
+        for _ in range(inner_steps):
+            loss = compute_loss(_suffix_logits(model, params, hid), tgt, msk)
+            grads = torch.autograd.grad(loss, [params[n] for n in fast], create_graph=create_graph,
+                                        retain_graph=create_graph)
+            params = dict(params)
+            for n, g in zip(fast, grads):
+                params[n] = params[n] - inner_lr * g
+        inner_losses.append(loss)
+    inner_loss = torch.stack(inner_losses).mean() if inner_losses else torch.zeros((), device=targets.device)
+    return params, inner_loss
+
+
 def meta_step(model: TTTModel, input_ids, targets, inner_mask, outer_mask, inner_lr: float, inner_steps: int,
               param_filter=None, chunk_size: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """(inner_loss, outer_loss) of one meta step; outer_loss.backward() gives the meta-gradient."""
     params: Dict[str, torch.Tensor] = dict(model.named_parameters())
     fast = _fast_names(model, param_filter)
     prefix = functional_call(model, params, (input_ids,), {"mode": "prefix"})
-
-    def suffix_logits(p, hidden):
-        return functional_call(model, p, (None,), {"mode": "suffix", "prefix_hidden": hidden})
-
-    inner_losses = []
-    for hid, tgt, msk in zip(_chunks(prefix, chunk_size), _chunks(targets, chunk_size), _chunks(inner_mask, chunk_size)):
-        for _ in range(inner_steps):
-            loss = compute_loss(suffix_logits(params, hid), tgt, msk)
-            grads = torch.autograd.grad(loss, [params[n] for n in fast], create_graph=True)
-            params = dict(params)
-            for n, g in zip(fast, grads):
-                params[n] = params[n] - inner_lr * g
-        inner_losses.append(loss)
-    inner_loss = torch.stack(inner_losses).mean() if inner_losses else torch.zeros((), device=targets.device)
-
+    params, inner_loss = _inner_scan(model, params, fast, prefix, targets, inner_mask, inner_lr, inner_steps,
+                                     chunk_size, create_graph=True)
     total, weight = torch.zeros((), device=targets.device), torch.zeros((), device=targets.device)
     for hid, tgt, msk in zip(_chunks(prefix, chunk_size), _chunks(targets, chunk_size), _chunks(outer_mask, chunk_size)):
         w = msk.sum()
         if w.item() <= 0:
             continue
-        total = total + compute_loss(suffix_logits(params, hid), tgt, msk) * w
+        total = total + compute_loss(_suffix_logits(model, params, hid), tgt, msk) * w
         weight = weight + w
     return inner_loss, total / weight.clamp_min(1.0)
+
+
+def ttt_apply(model: TTTModel, input_ids, targets, inner_mask, inner_lr: float, inner_steps: int,
+              param_filter=None, chunk_size: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Test-time adaptation at inference (cloud_ttt_e2e/ttt_e2e/meta.py:180-204): the
+    inner loop without create_graph; returns the adapted parameters by name. Each
+    inner step is an attention forward and first-order backward on the kernels."""
+    params: Dict[str, torch.Tensor] = dict(model.named_parameters())
+    fast = _fast_names(model, param_filter)
+    prefix = functional_call(model, params, (input_ids,), {"mode": "prefix"})
+    params, _ = _inner_scan(model, params, fast, prefix, targets, inner_mask, inner_lr, inner_steps, chunk_size,
+                            create_graph=False)
+    return params
+
+
+def ttt_logits(model: TTTModel, params: Dict[str, torch.Tensor], input_ids,
+               chunk_size: Optional[int] = None) -> torch.Tensor:
+    """Logits of the model with parameters ``params`` (cloud_ttt_e2e/ttt_e2e/meta.py:207-224):
+    the prefix over the whole sequence, the suffix over each chunk of it."""
+    prefix = functional_call(model, params, (input_ids,), {"mode": "prefix"})
+    return torch.cat([_suffix_logits(model, params, h) for h in _chunks(prefix, chunk_size)], dim=1)
+
+
+@torch.no_grad()
+def stream_logits(model: TTTModel, tokens: torch.Tensor, window_size: int, chunk_size: int) -> List[torch.Tensor]:
+    """Streaming inference as the reference's latency demo runs it
+    (cloud_ttt_e2e/scripts/demo_infer.py:11-27): for each chunk of ``chunk_size``
+    new tokens, one forward over the last ``window_size`` tokens up to the
+    chunk's end (forward-only attention on the kernels). Returns each call's logits."""
+    out = []
+    t = tokens.shape[1]
+    for start in range(0, t, chunk_size):
+        end = min(t, start + chunk_size)
+        out.append(model(tokens[:, max(0, end - window_size):end]))
+    return out
