@@ -162,9 +162,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // split mode: this CTA takes share `share` of its key block's query tiles
   const int nsplit = p.nsplit > 1 ? p.nsplit : 1;
-  const int bh = blockIdx.x / nsplit, share = blockIdx.x % nsplit;
+  const GridPos gp = grid_pos();
+  const int bh = gp.unit / nsplit, share = gp.unit % nsplit;
   const int bidx = bh / p.H, hidx = bh % p.H;
-  const int kblk = blockIdx.y;  // causal: small kblk has the most query tiles, launched first
+  const int kblk = gp.rank;  // causal: small kblk has the most query tiles, launched first
   const int k0 = kblk * BK;
   const int T = p.T;
   const int n_q = (T + BM - 1) / BM;

@@ -144,9 +144,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // split mode: this CTA takes share `share` of its query block's key tiles
   const int nsplit = p.nsplit > 1 ? p.nsplit : 1;
-  const int bh = blockIdx.x / nsplit, share = blockIdx.x % nsplit;
+  const GridPos gp = grid_pos();
+  const int bh = gp.unit / nsplit, share = gp.unit % nsplit;
   const int bidx = bh / p.H, hidx = bh % p.H;
-  const int qblk = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.y;
+  const int qblk = CAUSAL ? (gridDim.y - 1 - gp.rank) : gp.rank;  // longest rows first
   const int q0 = qblk * BM;
   const int T = p.T;
   const int n_all = (T + BN - 1) / BN;

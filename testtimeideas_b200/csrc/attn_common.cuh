@@ -64,6 +64,27 @@ struct KParams {
   float* part1;
 };
 
+// Launch order of a pass's CTAs, a grid of (units, blocks) with units = heads
+// (times split shares): units are taken kUnitGroup at a time and, within a
+// group, block rank by block rank, so that the CTAs running together share the
+// streamed tiles of a few heads in L2. (Taking every head's first block first
+// streams all heads' tiles at once, from DRAM, when there are many heads.)
+// Returns this CTA's unit and its block rank (rank 0 is launched first).
+constexpr int kUnitGroup = 4;
+struct GridPos {
+  int unit, rank;
+};
+TTT_DEV GridPos grid_pos() {
+  const int units = static_cast<int>(gridDim.x), nblk = static_cast<int>(gridDim.y);
+  const int64_t lin = blockIdx.x + static_cast<int64_t>(blockIdx.y) * gridDim.x;
+  const int64_t per_group = static_cast<int64_t>(kUnitGroup) * nblk;
+  const int group = static_cast<int>(lin / per_group);
+  const int base = group * kUnitGroup;
+  const int gs = min(kUnitGroup, units - base);
+  const int idx = static_cast<int>(lin - group * per_group);
+  return {base + idx % gs, idx / gs};
+}
+
 // Contiguous share `split` of `n` items cut into `nsplit` nearly equal parts.
 TTT_DEV int split_begin(int n, int split, int nsplit) {
   return static_cast<int>((static_cast<int64_t>(n) * split) / nsplit);
