@@ -421,6 +421,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       const float4* st_del = reinterpret_cast<const float4*>(statS(s, 1) + c0);
       const float4* st_gam = reinterpret_cast<const float4*>(statS(s, C::BWD2 ? 2 : 0) + c0);
       const float4* st_rho = reinterpret_cast<const float4*>(statS(s, C::BWD2 ? 3 : 0) + c0);
+      // causal: the loop runs in a masked and an unmasked version, so that
+      // interior tiles carry no per-element mask test
+      auto elementwise = [&](auto masked) {
 #pragma unroll
       for (int q4 = 0; q4 < CPW / 4; ++q4) {
         const float4 l4 = st_lse[q4], d4 = st_del[q4];
@@ -437,7 +440,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           float x0, x1;
           split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), L), x0, x1);
           float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          if (need_mask) {
+          if (static_cast<bool>(masked)) {
             const int qi = qcol0 + e;
             p0 = ((key < T) && (!CAUSAL || (key <= qi && qi <= key_hi))) ? p0 : 0.f;
             p1 = ((key < T) && (!CAUSAL || (key <= qi + 1 && qi + 1 <= key_hi))) ? p1 : 0.f;
@@ -452,12 +455,19 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             const F2 RHO = h2 ? f2(r4.z, r4.w) : f2(r4.x, r4.y);
             const F2 DPM = sub2(DP, DEL);
             const F2 GDS = mul2(f2(gd[e], gd[e + 1]), SC2);
-            const F2 GP = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), mul2(GAM, DP)));
+            const F2 GPR = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), fma2(GAM, DP, RHO)));  // G_P - rho
             split(mul2(PR, DPM), sv[e], sv[e + 1]);              // dS^T
-            split(mul2(PR, sub2(GP, RHO)), dp[e], dp[e + 1]);    // G_S^T
+            split(mul2(PR, GPR), dp[e], dp[e + 1]);              // G_S^T
             split(mul2(PR, sub2(GDS, GAM)), gd[e], gd[e + 1]);   // G_dP^T
           }
         }
+      }
+      };
+      if constexpr (CAUSAL) {
+        if (need_mask) elementwise(std::true_type{});
+        else elementwise(std::false_type{});
+      } else {
+        elementwise(need_mask);  // masks only a ragged last tile: one version
       }
       // A dedicated E region is reused every tile: wait until the previous tile's
       // accumulate products have read it. E over score columns needs no wait: the

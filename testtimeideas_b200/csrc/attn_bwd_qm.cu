@@ -35,6 +35,8 @@
 // results are written into the [V; u_v] part of their own stage, which only the
 // score products read. Causal: key tiles past the diagonal are skipped and only
 // boundary tiles are masked.
+#include <type_traits>
+
 #include "attn_pipe.cuh"
 #include "kernels.h"
 
@@ -432,12 +434,15 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       const int kt0 = (n_first + n) * BN;  // first key of the tile
       const int j0 = kt0 + c0;
       const bool need_mask = (kt0 + BN > T) || (CAUSAL && (kt0 + BN - 1 > q0 || band_edge > kt0));
+      // causal: the loop runs in a masked and an unmasked version, so that
+      // interior tiles carry no per-element mask test
+      auto elementwise = [&](auto masked) {
 #pragma unroll
       for (int e = 0; e < CPW; e += 2) {
         float x0, x1;
         split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), LSE2), x0, x1);
         float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-        if (need_mask) {
+        if (static_cast<bool>(masked)) {
           const int j = j0 + e;
           p0 = ((j < T) && (!CAUSAL || (j <= row && j >= row_lo))) ? p0 : 0.f;
           p1 = ((j + 1 < T) && (!CAUSAL || (j + 1 <= row && j + 1 >= row_lo))) ? p1 : 0.f;
@@ -454,13 +459,20 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         } else {
           const F2 DPM = sub2(DP, DEL2);
           const F2 GDS = mul2(f2(gd[e], gd[e + 1]), SC2);
-          const F2 GP = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), mul2(GAM2, DP)));
+          const F2 GPR = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), fma2(GAM2, DP, RHO2)));  // G_P - rho
           split(mul2(PR, DPM), sv[e], sv[e + 1]);                // dS
-          split(mul2(PR, sub2(GP, RHO2)), dp[e], dp[e + 1]);     // G_S
+          split(mul2(PR, GPR), dp[e], dp[e + 1]);                // G_S
           split(mul2(PR, sub2(GDS, GAM2)), gd[e], gd[e + 1]);    // G_dP
           uv[e] = p0;                                            // P
           uv[e + 1] = p1;
         }
+      }
+      };
+      if constexpr (CAUSAL) {
+        if (need_mask) elementwise(std::true_type{});
+        else elementwise(std::false_type{});
+      } else {
+        elementwise(need_mask);  // masks only a ragged last tile: one version
       }
       if constexpr (C::NE > 0) {
         // With EIS the results go into this tile's own stage (its score
