@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       gam = p.gamma[sidx];
       rho = p.rho[sidx];
     }
-    const F2 C2 = f2s(c), SC2 = f2s(scale), LSE2 = f2s(lse), DEL2 = f2s(del), GAM2 = f2s(gam), RHO2 = f2s(rho);
+    const F2 C2 = f2s(c), SC2 = f2s(scale), NLSE2 = f2s(-lse), DEL2 = f2s(del), GAM2 = f2s(gam), RHO2 = f2s(rho);
     F2 AG = f2s(0.f), A2 = AG, A3 = AG, A4 = AG;  // stats accumulators (column pairs)
     if constexpr (C::RES_TMEM) {
       // This thread's row, columns half*D/2 .. +D/2, of every operand kept in
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
 #pragma unroll
       for (int e = 0; e < CPW; e += 2) {
         float x0, x1;
-        split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), LSE2), x0, x1);
+        split(fma2(f2(sv[e], sv[e + 1]), C2, NLSE2), x0, x1);  // S c - lse2
         float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
         if (static_cast<bool>(masked)) {
           const int j = j0 + e;
@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
         if constexpr (KIND == kBwdQ) {
           split(mul2(PR, sub2(DP, DEL2)), sv[e], sv[e + 1]);
         } else if constexpr (KIND == kStats) {
-          const F2 TT = mul2(PR, mul2(f2(gd[e], gd[e + 1]), SC2));
+          const F2 TT = mul2(PR, f2(gd[e], gd[e + 1]));  // P G_dS / scale (scaled once per row below)
           AG = add2(AG, TT);
           A2 = fma2(TT, DP, A2);
           A4 = fma2(PR, DP, A4);
@@ -496,9 +496,9 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
     if constexpr (KIND == kStats) {
       float a_g, a2, a3, a4, hi_;
       split(AG, a_g, hi_);
-      a_g += hi_;
+      a_g = (a_g + hi_) * scale;
       split(A2, a2, hi_);
-      a2 += hi_;
+      a2 = (a2 + hi_) * scale;
       split(A3, a3, hi_);
       a3 += hi_;
       split(A4, a4, hi_);
