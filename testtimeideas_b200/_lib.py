@@ -165,11 +165,11 @@ def prep(x: torch.Tensor) -> torch.Tensor:
     (d stride != 1, a stride not a multiple of 8 elements, or a misaligned base)."""
     if x.dim() != 4:
         raise ValueError(f"expected a [b, h, t, d] tensor, got shape {tuple(x.shape)}")
-    b, h, t, d = x.shape
-    ok = x.stride(3) == 1 and x.data_ptr() % 16 == 0
+    shape, st = x.shape, x.stride()
+    ok = st[3] == 1 and x.data_ptr() % 16 == 0
     if ok:
-        for size, stride in ((b, x.stride(0)), (h, x.stride(1)), (t, x.stride(2))):
-            if size > 1 and (stride <= 0 or stride % 8 != 0):
+        for i in range(3):
+            if shape[i] > 1 and (st[i] <= 0 or st[i] % 8 != 0):
                 ok = False
     return x if ok else x.contiguous()
 
@@ -177,7 +177,8 @@ def prep(x: torch.Tensor) -> torch.Tensor:
 def view(x: torch.Tensor | None) -> View:
     if x is None:
         return View(None, 0, 0, 0)
-    return View(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2))
+    st = x.stride()
+    return View(x.data_ptr(), st[0], st[1], st[2])
 
 
 WINDOW_KINDS = {"sliding": 0, "chunk": 1}
@@ -217,6 +218,25 @@ def work_space(pb: Problem, device: torch.device):
     return buf, buf.data_ptr(), n
 
 
+class _on:
+    """Make `device` current for the block; a no-op when it already is (the common
+    case, cheaper than torch.cuda.device)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.prev)
+
+
 def _stream() -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -232,7 +252,7 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: 
     lib = load_library()
     q, k, v = prep(q), prep(k), prep(v)
     b, h, t, d = q.shape
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         o = torch.empty((b, h, t, d), dtype=q.dtype, device=q.device)
         lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         # causal: the kernel writes only key tiles up to the diagonal; the rest stays zero
@@ -253,7 +273,7 @@ def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0
     lib = load_library()
     q, k, v, o, dout = prep(q), prep(k), prep(v), prep(o), prep(dout.to(q.dtype))
     b, h, t, d = q.shape
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         dq, dk, dv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
         delta = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         pb = problem(q, causal, scale, window)
@@ -285,7 +305,7 @@ def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float
 
     uq, uk, uv = probe(uq), probe(uk), probe(uv)
     b, h, t, d = q.shape
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         gq, gk, gv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
         gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
         gamma = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
@@ -338,7 +358,7 @@ def attn_bwd2_noalloc(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scal
     lib = load_library()
     q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
     uq, uk, uv = (prep(u.to(q.dtype)) for u in (uq, uk, uv))
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         gq, gk, gv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
         gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
         args = Bwd2Args(problem(q, causal, scale), view(q), view(k), view(v), view(dout), lse2.data_ptr(),
@@ -435,7 +455,7 @@ def dqdk_from_p(q, k, v, dout, p, rowsum, causal: bool, scale: float):
     p = prep_p(p.to(q.dtype))
     b, h, t, _ = q.shape
     rs = rowsum.reshape(b * h, t).to(torch.float32).contiguous()
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         dq, dk = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(2))
         args = _from_p_args(p, q, causal, scale, q=q, k=k, v=v, dout=dout, rowsum=rs, dq=dq, dk=dk)
         _check(lib.ttt_attn_dqdk_from_p(ctypes.byref(args), _stream()))
