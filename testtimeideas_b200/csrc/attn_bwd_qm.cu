@@ -59,7 +59,13 @@ struct QmCfg {
   // it removes the small d=64 spills but the idle warps cost more (measured
   // 0.8-1.2% slower per step).
   static constexpr bool SPLIT_REGS = false;
-  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64);
+  // Two MMA issuing threads: one issuing thread cannot feed the tensor pipe at
+  // its rate (measured on B200: ~85 cycles per UMMA from one thread; two
+  // threads reach the pipe's ~50 cycles for N=64 and ~65 for N=128). Issuer 0
+  // takes the score products, issuer 1 the accumulate products; without
+  // accumulate products (statistics pass) they take alternate tiles.
+  static constexpr bool TWO_ISSUERS = true;
+  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0);
   static constexpr int REG_LAUNCH = 168, REG_CTRL = 152, REG_ELEM = (3 * REG_LAUNCH - REG_CTRL) / 2;
   static_assert(REG_ELEM % 8 == 0 && 2 * REG_ELEM + REG_CTRL <= 3 * REG_LAUNCH, "register split");
   static constexpr int CPW = BN / 2;
@@ -92,7 +98,7 @@ struct QmCfg {
   static constexpr int OFF_S = OFF_R + NR_SMEM * TILE_R;
   static constexpr int OFF_E = OFF_S + NSTAGE * STAGE;
   static constexpr int OFF_BAR = OFF_E + E_BYTES;
-  static constexpr int NBAR = 17;
+  static constexpr int NBAR = 18;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "query-major tile set exceeds shared memory");
   // TMEM column offsets of the score tiles within one buffer
@@ -106,7 +112,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   using C = QmCfg<D, KIND, GDO>;
   constexpr int BM = C::BM, BN = C::BN, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE, CPW = C::CPW;
   constexpr int SR = C::ST_ROWS;
-  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1;
+  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1, WARP_MMA2 = C::NCW + 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sR = smem + C::OFF_R;
@@ -129,10 +135,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   uint64_t* e_full = bars + 13;  // [2] compute -> MMA
   uint64_t* e_empty = bars + 15; // MMA -> compute
   uint64_t* acc_full = bars + 16;
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* drain = bars + 17;  // [2] one per MMA issuer (bars + 18 for the second)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  static_assert(18 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
+  static_assert(19 * 8 + 8 <= C::NBAR * 8 + 16, "barrier area");
   // resident tiles kept in shared memory, packed in slot order
   auto in_tmem = [&](int t) { return (t == 0 && C::RT_Q) || (t == 1 && C::RT_DO) || (t == 2 && C::RT_UQ); };
   auto tileR = [&](int t) {
@@ -161,7 +167,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const int n_tiles = n_lo + split_begin(n_hi - n_lo, share + 1, nsplit) - n_first;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 19; ++i) mbar_init(bars + i, 1);
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     mbar_init(e_full + 0, C::NCT);
@@ -220,8 +226,8 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-   } else if (warp == WARP_MMA) {
-    // ------------------------------------------------------------ MMA issuer
+   } else if (warp == WARP_MMA || (C::TWO_ISSUERS && warp == WARP_MMA2)) {
+    // ------------------------------------------------------------ MMA issuer(s)
     if (lane == 0) {
       constexpr uint32_t id_n1 = idesc_f16(128, BN, BF16, false, false);
       constexpr uint32_t id_n2 = idesc_f16(128, 2 * BN, BF16, false, false);
@@ -313,47 +319,74 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       bool ok = mbar_wait(res_full, 0, g, 1);
       // res_full's phase 0 completed above: a probe of it always succeeds (an unused probe slot)
       const uint64_t* done = res_full;
-      bool have_l = false, have_s = false;  // the next score step's barriers already seen complete
-      for (int n = 0; ok && n < n_tiles; ++n) {
-        const int sb = n % NBUF, s = n % NSTAGE;
-        if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
-        if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
-        tc_fence_after();
-        // barriers of tile n+1's score step
-        const bool nxt = n + 1 < n_tiles;
-        const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
-        const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
-        const bool need_s = nxt && n + 1 >= NBUF;
-        const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
-        const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
-        if (C::NA > 0 && n >= 1) {
-          // tile n-1's accumulate step follows: probe its e_full while issuing these scores
-          uint64_t* be = e_full + ((n - 1) & 1);
-          const uint32_t pe = ((n - 1) >> 1) & 1;
-          const uint32_t seen = issue_scores(n, be, pe, bl, pl);
-          if (!(seen & 1) && !(ok = mbar_wait(be, pe, g, 4))) break;
-          tc_fence_after();
-          const uint32_t seen2 = issue_acc(n - 1, bl, pl, bs, ps);
-          have_l = ((seen >> 1) & 1) || (seen2 & 1);
-          have_s = (seen2 >> 1) & 1;
-        } else {
-          const uint32_t seen = issue_scores(n, bl, pl, bs, ps);
-          have_l = seen & 1;
-          have_s = (seen >> 1) & 1;
-        }
-      }
-      if constexpr (C::NA > 0) {
-        if (ok && n_tiles > 0) {
-          ok = mbar_wait(e_full + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, g, 4);
-          if (ok) {
+      if constexpr (C::TWO_ISSUERS) {
+        const int me = warp == WARP_MMA ? 0 : 1;
+        if (C::NA == 0 || me == 0) {
+          // score products: of every tile (issuer 0), or of alternate tiles, each in its
+          // own score buffer (statistics pass)
+          const int step = C::NA == 0 ? 2 : 1;
+          for (int n = C::NA == 0 ? me : 0; ok && n < n_tiles; n += step) {
+            const int sb = n % NBUF, s = n % NSTAGE;
+            if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
             tc_fence_after();
-            issue_acc(n_tiles - 1, done, 0u, done, 0u);
+            issue_scores(n, done, 0u, done, 0u);
+          }
+        } else {
+          // accumulate products of every tile, once its elementwise results are written
+          // (tile n's score products completed before that: its stage may then be refilled)
+          for (int n = 0; ok && n < n_tiles; ++n) {
+            if (!(ok = mbar_wait(e_full + (n & 1), (n >> 1) & 1, g, 4))) break;
+            tc_fence_after();
+            issue_acc(n, done, 0u, done, 0u);
+          }
+          if (ok) umma_commit(acc_full);
+        }
+        umma_commit(drain + me);
+        mbar_drain(drain + me, 0);
+      } else {
+        bool have_l = false, have_s = false;  // the next score step's barriers already seen complete
+        for (int n = 0; ok && n < n_tiles; ++n) {
+          const int sb = n % NBUF, s = n % NSTAGE;
+          if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+          if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+          tc_fence_after();
+          // barriers of tile n+1's score step
+          const bool nxt = n + 1 < n_tiles;
+          const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
+          const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
+          const bool need_s = nxt && n + 1 >= NBUF;
+          const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
+          const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
+          if (C::NA > 0 && n >= 1) {
+            // tile n-1's accumulate step follows: probe its e_full while issuing these scores
+            uint64_t* be = e_full + ((n - 1) & 1);
+            const uint32_t pe = ((n - 1) >> 1) & 1;
+            const uint32_t seen = issue_scores(n, be, pe, bl, pl);
+            if (!(seen & 1) && !(ok = mbar_wait(be, pe, g, 4))) break;
+            tc_fence_after();
+            const uint32_t seen2 = issue_acc(n - 1, bl, pl, bs, ps);
+            have_l = ((seen >> 1) & 1) || (seen2 & 1);
+            have_s = (seen2 >> 1) & 1;
+          } else {
+            const uint32_t seen = issue_scores(n, bl, pl, bs, ps);
+            have_l = seen & 1;
+            have_s = (seen >> 1) & 1;
           }
         }
-        if (ok) umma_commit(acc_full);
+        if constexpr (C::NA > 0) {
+          if (ok && n_tiles > 0) {
+            ok = mbar_wait(e_full + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, g, 4);
+            if (ok) {
+              tc_fence_after();
+              issue_acc(n_tiles - 1, done, 0u, done, 0u);
+            }
+          }
+          if (ok) umma_commit(acc_full);
+        }
+        umma_commit(drain);
+        mbar_drain(drain, 0);
       }
-      umma_commit(drain);
-      mbar_drain(drain, 0);
     }
    }
   } else {
