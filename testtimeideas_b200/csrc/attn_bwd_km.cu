@@ -65,7 +65,6 @@ struct KmCfg {
   // Off: with it the share bookkeeping of split mode fits without small spills,
   // but the two idle warps cost more (measured 0.7-1.6% slower per step).
   static constexpr bool SPLIT_REGS = false;
-  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64);  // + the control warpgroup
   // Register split: the launch gives every thread REG_LAUNCH registers (three
   // warps share one 16K-register sub-partition); the control warpgroup then
   // drops to REG_CTRL and the two elementwise warpgroups rise to REG_ELEM.
@@ -91,12 +90,18 @@ struct KmCfg {
   static constexpr int ACC_COL = SC_COLS;
   static constexpr bool E_DEDICATED = ETM && (SC_COLS + NA * D + NE * E_COLS <= 512);
   static constexpr bool E_OVERLAP = ETM && !E_DEDICATED;  // E shares score columns 0 .. NE*E_COLS
+  // Two MMA issuing threads (one thread cannot feed the tensor pipe at its
+  // rate): issuer 0 the score products, issuer 1 the accumulate products. Not
+  // with E over the first score tile's columns (d=128 double backward), where
+  // the next tile's products must follow the previous accumulate products.
+  static constexpr bool TWO_ISSUERS = !E_OVERLAP;
+  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0);
   static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : 0;
   static constexpr int TMEM_USED = SC_COLS + NA * D + (E_DEDICATED ? NE * E_COLS : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
   static_assert(!E_OVERLAP || NBUF == 1, "overlapping E needs a single score buffer");
-  static constexpr int BAR_BYTES = 20 * 8;
+  static constexpr int BAR_BYTES = 22 * 8;
   static constexpr int FIXED = NR * TILE_R + BAR_BYTES + (STAGE_TX - STAGE);
   static constexpr int NSTAGE = (FIXED + 4 * STAGE + 1024 <= 232448) ? 4 : (FIXED + 3 * STAGE + 1024 <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
@@ -124,7 +129,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   using C = KmCfg<D, KIND>;
   constexpr int BM = C::BM, BK = C::BK, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE, CPW = C::CPW;
   constexpr int SR0 = C::ST0_ROWS;
-  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1;
+  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1, WARP_MMA2 = C::NCW + 2;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = C::PAD ? align1024(smem_raw) : smem_raw;
   if (C::PAD == 0 && (smem_u32(smem_raw) & 1023u) != 0) {
@@ -149,8 +154,11 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   uint64_t* e_full = bars + 13;   // [2]
   uint64_t* e_empty = bars + 15;  // accumulate products of a tile finished (E consumed)
   uint64_t* acc_full = bars + 16;
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* drain = bars + 17;   // [2] one per MMA issuer (bars + 18 for the second)
+  // e_cons[b]: the accumulate products that read E in score buffer b completed
+  // (two issuers, E over its own score buffer)
+  uint64_t* e_cons = bars + 19;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto tileR = [&](int t) { return sR + t * C::TILE_R; };
   auto st0 = [&](int s) { return sS + s * C::STAGE; };
@@ -178,7 +186,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const int n_tiles = qt_first + split_begin(qt_end - qt_first, share + 1, nsplit) - qt0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 18; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 21; ++i) mbar_init(bars + i, 1);
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     mbar_init(e_full + 0, C::NCT);
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-   } else if (warp == WARP_MMA) {
+   } else if (warp == WARP_MMA || (C::TWO_ISSUERS && warp == WARP_MMA2)) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_n1 = idesc_f16(128, BM, BF16, false, false);
@@ -320,57 +328,90 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       bool ok = mbar_wait(res_full, 0, g, 1);
       // res_full's phase 0 completed above: a probe of it always succeeds (an unused probe slot)
       const uint64_t* done = res_full;
-      bool have_l = false, have_s = false;  // this tile's l_full / s_free already seen complete by a probe
-      for (int n = 0; ok && n <= n_tiles; ++n) {
-        const bool has_scores = n < n_tiles;
-        const int sb = n % NBUF, s = n % NSTAGE;
-        const uint32_t base = tmem + sb * C::NSC * BM;
-        // barriers of tile n+1's score products, probed while this iteration issues
-        const bool nxt = n + 1 < n_tiles;
-        const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
-        const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
-        const bool need_s = nxt && n + 1 >= NBUF;
-        const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
-        const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
-        const uint64_t* be = n >= 1 ? e_full + ((n - 1) & 1) : done;
-        const uint32_t pe = n >= 1 ? ((n - 1) >> 1) & 1 : 0u;
-        bool next_l = false, next_s = false, seen_e = false;
-        if (has_scores) {
-          if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
-          if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
-          tc_fence_after();
-          if constexpr (!C::E_OVERLAP) scores_e_cols(base, s, done, 0u, done, 0u);
-          const uint32_t seen = scores_free_cols(base, s, be, pe, bl, pl);
-          if constexpr (!C::E_OVERLAP) umma_commit(s_full + sb);
-          seen_e = seen & 1;
-          next_l = (seen >> 1) & 1;
-        }
-        if (n >= 1) {
-          // accumulate products of tile n-1
-          if (!seen_e && !(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
-          tc_fence_after();
-          const uint32_t seen = acc_products(n - 1, bl, pl, bs, ps);
-          if constexpr (C::E_DEDICATED) umma_commit(e_empty);
-          umma_commit(l_empty + (n - 1) % NSTAGE);
-          next_l = next_l || (seen & 1);
-          next_s = (seen >> 1) & 1;
-        }
-        if constexpr (C::E_OVERLAP) {
-          if (has_scores) {
-            // overwrites the columns of E(n-1), which the products just issued read first
-            // (tile n+1 also needs s_free(n), which cannot be complete before these scores are)
-            const uint32_t seen = scores_e_cols(base, s, bl, pl, done, 0u);
+      if constexpr (C::TWO_ISSUERS) {
+        const int me = warp == WARP_MMA ? 0 : 1;
+        if (me == 0) {
+          // score products of every tile
+          for (int n = 0; ok && n < n_tiles; ++n) {
+            const int sb = n % NBUF, s = n % NSTAGE;
+            const uint32_t base = tmem + sb * C::NSC * BM;
+            if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+            // E over its own score buffer: the accumulate products that read it completed
+            if (C::E_OWN && n >= NBUF && !(ok = mbar_wait(e_cons + sb, ((n / NBUF) - 1) & 1, g, 5))) break;
+            tc_fence_after();
+            scores_e_cols(base, s, done, 0u, done, 0u);
+            scores_free_cols(base, s, done, 0u, done, 0u);
             umma_commit(s_full + sb);
-            next_l = next_l || (seen & 1);
-            next_s = next_s || ((seen >> 1) & 1);
           }
+        } else {
+          // accumulate products of every tile, once its E is written (its score products
+          // completed before that, so its stage may be refilled afterwards)
+          for (int n = 0; ok && n < n_tiles; ++n) {
+            if (!(ok = mbar_wait(e_full + (n & 1), (n >> 1) & 1, g, 4))) break;
+            tc_fence_after();
+            acc_products(n, done, 0u, done, 0u);
+            if constexpr (C::E_DEDICATED) umma_commit(e_empty);
+            if constexpr (C::E_OWN) umma_commit(e_cons + n % NBUF);
+            umma_commit(l_empty + n % NSTAGE);
+          }
+          if (ok) umma_commit(acc_full);
         }
-        have_l = next_l;
-        have_s = next_s;
+        umma_commit(drain + me);
+        mbar_drain(drain + me, 0);
+      } else {
+        bool have_l = false, have_s = false;  // this tile's l_full / s_free already seen complete by a probe
+        for (int n = 0; ok && n <= n_tiles; ++n) {
+          const bool has_scores = n < n_tiles;
+          const int sb = n % NBUF, s = n % NSTAGE;
+          const uint32_t base = tmem + sb * C::NSC * BM;
+          // barriers of tile n+1's score products, probed while this iteration issues
+          const bool nxt = n + 1 < n_tiles;
+          const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
+          const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
+          const bool need_s = nxt && n + 1 >= NBUF;
+          const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
+          const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
+          const uint64_t* be = n >= 1 ? e_full + ((n - 1) & 1) : done;
+          const uint32_t pe = n >= 1 ? ((n - 1) >> 1) & 1 : 0u;
+          bool next_l = false, next_s = false, seen_e = false;
+          if (has_scores) {
+            if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+            tc_fence_after();
+            if constexpr (!C::E_OVERLAP) scores_e_cols(base, s, done, 0u, done, 0u);
+            const uint32_t seen = scores_free_cols(base, s, be, pe, bl, pl);
+            if constexpr (!C::E_OVERLAP) umma_commit(s_full + sb);
+            seen_e = seen & 1;
+            next_l = (seen >> 1) & 1;
+          }
+          if (n >= 1) {
+            // accumulate products of tile n-1
+            if (!seen_e && !(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
+            tc_fence_after();
+            const uint32_t seen = acc_products(n - 1, bl, pl, bs, ps);
+            if constexpr (C::E_DEDICATED) umma_commit(e_empty);
+            umma_commit(l_empty + (n - 1) % NSTAGE);
+            next_l = next_l || (seen & 1);
+            next_s = (seen >> 1) & 1;
+          }
+          if constexpr (C::E_OVERLAP) {
+            if (has_scores) {
+              // overwrites the columns of E(n-1), which the products just issued read first
+              // (tile n+1 also needs s_free(n), which cannot be complete before these scores are)
+              const uint32_t seen = scores_e_cols(base, s, bl, pl, done, 0u);
+              umma_commit(s_full + sb);
+              next_l = next_l || (seen & 1);
+              next_s = next_s || ((seen >> 1) & 1);
+            }
+          }
+          have_l = next_l;
+          have_s = next_s;
+        }
+        if (ok) umma_commit(acc_full);
+        umma_commit(drain);
+        mbar_drain(drain, 0);
       }
-      if (ok) umma_commit(acc_full);
-      umma_commit(drain);
-      mbar_drain(drain, 0);
     }
    }
   } else {
