@@ -99,6 +99,10 @@ struct KmCfg {
   // (S^T, G_dS^T), issuer 1 the others (dP^T, (dO u_v^T)^T) and the accumulates.
   // Measured: 8% faster for the d=128 backward, no gain or a loss at d=64.
   static constexpr bool SPLIT_SCORES = TWO_ISSUERS && D == 128;
+  // First-order d=128: issuer 1 would issue dP^T and both accumulates (16 UMMAs
+  // a tile) against issuer 0's 8 for S^T, so issuer 0 also takes dV += P^T dO;
+  // a stage is then released by both (l_empty and acc_full count two commits).
+  static constexpr bool ACC_SPLIT = SPLIT_SCORES && !BWD2;
   static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0);
   static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : 0;
   static constexpr int TMEM_USED = SC_COLS + NA * D + (E_DEDICATED ? NE * E_COLS : 0);
@@ -196,6 +200,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     if (C::SPLIT_SCORES) {  // both issuers' score products
       mbar_init(s_full + 0, 2);
       mbar_init(s_full + 1, 2);
+    }
+    if (C::ACC_SPLIT) {  // both issuers' accumulate products
+      for (int i = 0; i < 4; ++i) mbar_init(l_empty + i, 2);
+      mbar_init(acc_full, 2);
     }
     mbar_init(e_full + 0, C::NCT);
     mbar_init(e_full + 1, C::NCT);
@@ -307,15 +315,19 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
                                       p0_, b1_, p1_);
         }
       };
-      auto acc_products = [&](int n, const uint64_t* b0_, uint32_t p0_, const uint64_t* b1_, uint32_t p1_) -> uint32_t {
+      // parts (first-order kernel): bit 0 dV += P^T dO, bit 1 dK += dS^T Q
+      auto acc_products = [&](int n, const uint64_t* b0_, uint32_t p0_, const uint64_t* b1_, uint32_t p1_,
+                              int parts = 3) -> uint32_t {
         const int s = n % NSTAGE;
         const uint32_t bQ = smem_u32(st0(s)), bDO = smem_u32(st1(s));
         const uint32_t acc_first = n > 0 ? 1u : 0u;
         if constexpr (!C::BWD2) {
-          // dV += P^T dO ; dK += dS^T Q
+          if (parts & 1) {
 #pragma unroll
-          for (int kk = 0; kk < BM / 16; ++kk)
-            umma_ts(tAcc1, e_col(0, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, (acc_first || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BM / 16; ++kk)
+              umma_ts(tAcc1, e_col(0, kk, n), desc_mnmajor(bDO, BM, kk), id_acc, (acc_first || kk > 0) ? 1u : 0u);
+          }
+          if (!(parts & 2)) return 0u;
           return issue_ts<BM / 16, LE, PR>(tAcc0, e_col(1, 0, n), desc_mnmajor(bQ, SR0, 0), id_acc, acc_first, b0_, p0_,
                                        b1_, p1_);
         } else {
@@ -342,7 +354,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         // columns E may use; issuer 1 the others, both committing s_full, which then
         // counts two arrivals); issuer 1: each tile's accumulate products once its E is
         // written (its score products completed before that, so its stage may be
-        // refilled afterwards)
+        // refilled afterwards); with ACC_SPLIT issuer 0 takes the dV products of the tile
         for (int n = 0; ok && n <= n_tiles; ++n) {
           if (n < n_tiles && (me == 0 || C::SPLIT_SCORES)) {
             const int sb = n % NBUF, s = n % NSTAGE;
@@ -357,16 +369,19 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             if (me == 1 || !C::SPLIT_SCORES) scores_free_cols(base, s, done, 0u, done, 0u);
             umma_commit(s_full + sb);
           }
-          if (me == 1 && n >= 1) {
+          if ((me == 1 || C::ACC_SPLIT) && n >= 1) {
             if (!(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
             tc_fence_after();
-            acc_products(n - 1, done, 0u, done, 0u);
+            acc_products(n - 1, done, 0u, done, 0u, C::ACC_SPLIT ? (me == 0 ? 1 : 2) : 3);
             if constexpr (C::E_DEDICATED) umma_commit(e_empty);
-            if constexpr (C::E_OWN) umma_commit(e_cons + (n - 1) % NBUF);
+            // issuer 0's own score products into this buffer follow its dV products in order
+            if constexpr (C::E_OWN) {
+              if (me == 1) umma_commit(e_cons + (n - 1) % NBUF);
+            }
             umma_commit(l_empty + (n - 1) % NSTAGE);
           }
         }
-        if (me == 1 && ok) umma_commit(acc_full);
+        if ((me == 1 || C::ACC_SPLIT) && ok) umma_commit(acc_full);
         umma_commit(drain + me);
         mbar_drain(drain + me, 0);
       } else {
@@ -478,7 +493,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
 #pragma unroll
       for (int q4 = 0; q4 < CPW / 4; ++q4) {
         const float4 l4 = st_lse[q4], d4 = st_del[q4];
-        float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), r4 = g4;
+        [[maybe_unused]] float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), r4 = g4;  // double backward only
         if constexpr (C::BWD2) {
           g4 = st_gam[q4];
           r4 = st_rho[q4];
