@@ -12,12 +12,12 @@
 //             reference approximates with torch.matmul in
 //             backward_stubs.py:435-514)
 //
-// Roles (320 threads): warps 0..7 elementwise (warp w: TMEM lanes
-// 32*(w%4)..+31, tile columns (w/4)*32..+32), warp 8 MMA issuer, warp 9 TMA
-// producer (with SPLIT_REGS, 384 threads: warps 10-11 idle complete the control
-// warpgroup, which gives registers to the elementwise warpgroups with
-// setmaxnreg). The per-query statistics (lse2, delta, gamma, rho) of each tile
-// arrive with it through TMA and are read with broadcast 16-byte loads.
+// Roles: warps 0..7 elementwise (warp w: TMEM lanes 32*(w%4)..+31, tile
+// columns (w/4)*32..+32), warp 9 TMA producer, warps 8 and 10 (and 11) MMA
+// issuers: one thread issues at most one tcgen05.mma per ~85 cycles, below the
+// tensor pipe's rate. The per-query statistics (lse2, delta, gamma, rho) of
+// each tile arrive with it through TMA and are read with broadcast 16-byte
+// loads.
 //
 // The elementwise results E (16-bit P^T, dS^T | dS^T, G_S^T, G_dP^T) live in
 // TMEM as packed pairs and are the A operand of the accumulate products:
@@ -26,13 +26,14 @@
 //     S^T columns take its 16 P^T and 16 dS^T words);
 //   kBwd2KV d=64: a dedicated region;
 //   kBwd2KV d=128, where four 64-wide score tiles and two 128-wide
-//     accumulators fill all 512 columns: columns shared with the first score
-//     tiles. Each tile first issues the score products that do not touch them
-//     (dP^T, (dO u_v^T)^T), then the previous tile's accumulate products, then
-//     the products that overwrite the shared columns (K [Q; u_q]^T, u_k Q^T).
+//     accumulators fill all 512 columns: dS^T and G_S^T over the dP^T columns,
+//     G_dP^T over the (dO u_v^T)^T columns. Three issuers: issuer 0 the
+//     products over S^T and G_dS^T (K [Q; u_q]^T, u_k Q^T), which no longer
+//     wait for E; issuer 1 the dd_K products of tile n, then dP^T of tile n+1;
+//     issuer 2 the dd_V products of tile n, then (dO u_v^T)^T of tile n+1.
 // Reusing E's columns for the next score product needs no wait: tcgen05.mma
 // ops issued by one thread execute in issue order, so the accumulate product
-// has read E before a later product writes there.
+// has read E before a later product of the same thread writes there.
 //
 // In the double backward the streamed Q and u_q tiles are stacked in one
 // panel so that K [Q; u_q]^T produces [S^T | K u_q^T] as a single N=128
@@ -89,11 +90,17 @@ struct KmCfg {
   static constexpr int SC_COLS = NBUF * NSC * BM;
   static constexpr int ACC_COL = SC_COLS;
   static constexpr bool E_DEDICATED = ETM && (SC_COLS + NA * D + NE * E_COLS <= 512);
-  static constexpr bool E_OVERLAP = ETM && !E_DEDICATED;  // E shares score columns 0 .. NE*E_COLS
+  // E over score columns (d=128 double backward): E tiles 0 and 1 (read by the
+  // dd_K products) over the dP^T columns, E tile 2 (read by dd_V) over the
+  // (dO u_v^T)^T columns, so the S^T / G_dS^T products never wait for E.
+  static constexpr bool E_OVERLAP = ETM && !E_DEDICATED;
   // Two MMA issuing threads (one thread cannot feed the tensor pipe at its
-  // rate): issuer 0 the score products, issuer 1 the accumulate products. Not
-  // with E over the first score tile's columns (d=128 double backward), where
-  // the next tile's products must follow the previous accumulate products.
+  // rate): issuer 0 the score products, issuer 1 the accumulate products. With
+  // E over score columns, three: issuer 0 the S^T / G_dS^T products, issuer 1
+  // the dd_K products of tile n then the dP^T product of tile n+1 over the same
+  // columns, issuer 2 the dd_V products then (dO u_v^T)^T; every product that
+  // overwrites E follows the products that read it on the same thread.
+  static constexpr bool THREE_ISSUERS = E_OVERLAP;
   static constexpr bool TWO_ISSUERS = !E_OVERLAP;
   // Split the score products too: issuer 0 those over the columns E may use
   // (S^T, G_dS^T), issuer 1 the others (dP^T, (dO u_v^T)^T) and the accumulates.
@@ -103,8 +110,10 @@ struct KmCfg {
   // a tile) against issuer 0's 8 for S^T, so issuer 0 also takes dV += P^T dO;
   // a stage is then released by both (l_empty and acc_full count two commits).
   static constexpr bool ACC_SPLIT = SPLIT_SCORES && !BWD2;
-  static constexpr int NTHREADS = NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0);
-  static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : 0;
+  static constexpr int NTHREADS =
+      NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0) + (THREE_ISSUERS ? 64 : 0);
+  static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : (E_OVERLAP ? 2 * BM : 0);
+  static_assert(!E_OVERLAP || BWD2, "E over score columns only in the double backward");
   static constexpr int TMEM_USED = SC_COLS + NA * D + (E_DEDICATED ? NE * E_COLS : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
@@ -137,7 +146,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   using C = KmCfg<D, KIND>;
   constexpr int BM = C::BM, BK = C::BK, NP = D / 64, NBUF = C::NBUF, NSTAGE = C::NSTAGE, CPW = C::CPW;
   constexpr int SR0 = C::ST0_ROWS;
-  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1, WARP_MMA2 = C::NCW + 2;
+  constexpr int WARP_MMA = C::NCW, WARP_LOAD = C::NCW + 1, WARP_MMA2 = C::NCW + 2, WARP_MMA3 = C::NCW + 3;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = C::PAD ? align1024(smem_raw) : smem_raw;
   if (C::PAD == 0 && (smem_u32(smem_raw) & 1023u) != 0) {
@@ -162,7 +171,9 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   uint64_t* e_full = bars + 13;   // [2]
   uint64_t* e_empty = bars + 15;  // accumulate products of a tile finished (E consumed)
   uint64_t* acc_full = bars + 16;
-  uint64_t* drain = bars + 17;   // [2] one per MMA issuer (bars + 18 for the second)
+  // one per MMA issuer: bars + 17, 18 (and 19, the e_cons slot, for a third:
+  // three issuers only with E over score columns, where e_cons is unused)
+  uint64_t* drain = bars + 17;
   // e_cons[b]: the accumulate products that read E in score buffer b completed
   // (two issuers, E over its own score buffer)
   uint64_t* e_cons = bars + 19;  // [2]
@@ -205,6 +216,11 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       for (int i = 0; i < 4; ++i) mbar_init(l_empty + i, 2);
       mbar_init(acc_full, 2);
     }
+    if (C::THREE_ISSUERS) {  // all three read a stage and write score columns
+      mbar_init(s_full, 3);
+      for (int i = 0; i < 4; ++i) mbar_init(l_empty + i, 3);
+      mbar_init(acc_full, 2);  // issuers 1 and 2
+    }
     mbar_init(e_full + 0, C::NCT);
     mbar_init(e_full + 1, C::NCT);
     // A nonzero error word means an earlier CTA or launch gave up: exit at once.
@@ -227,13 +243,14 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   Guard g{abort_flag, p.err};
   // TMEM column of K-step kk (16 queries) of E tile j of tile n. Outside a
   // dedicated region each half of the elementwise warps (queries 32h..32h+31)
-  // writes E only over score columns it has read itself: the first score tile's
-  // 32 columns take E tiles 0 and 1 (16 words each), the second's take tile 2.
+  // writes E only over score columns it has read itself: 32 columns of the first
+  // score tile it covers take E tiles 0 and 1 (16 words each), 32 of the second
+  // take tile 2 (first order: S^T; double backward: dP^T, then (dO u_v^T)^T).
   auto e_col = [&](int j, int kk, int n) -> uint32_t {
     if constexpr (C::E_DEDICATED) return tE + j * C::E_COLS + kk * 8;
     const uint32_t off = 32 * (kk >> 1) + (kk & 1) * 8 + (j == 2 ? BM : 16 * j);
     if constexpr (C::E_OWN) return tmem + (n % NBUF) * C::NSC * BM + off;
-    return tmem + off;
+    return tE + off;
   };
 
   if (warp >= C::NCW) {
@@ -269,7 +286,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       for (int s = 0; s < NSTAGE; ++s)
         if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
     }
-   } else if (warp == WARP_MMA || (C::TWO_ISSUERS && warp == WARP_MMA2)) {
+   } else if (warp == WARP_MMA || ((C::TWO_ISSUERS || C::THREE_ISSUERS) && warp == WARP_MMA2) ||
+              (C::THREE_ISSUERS && warp == WARP_MMA3)) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_n1 = idesc_f16(128, BM, BF16, false, false);
@@ -385,57 +403,57 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         umma_commit(drain + me);
         mbar_drain(drain + me, 0);
       } else {
-        bool have_l = false, have_s = false;  // this tile's l_full / s_free already seen complete by a probe
+        // three issuers, E over the dP^T and (dO u_v^T)^T columns (single score buffer)
+        const int me = warp == WARP_MMA ? 0 : (warp == WARP_MMA2 ? 1 : 2);
         for (int n = 0; ok && n <= n_tiles; ++n) {
-          const bool has_scores = n < n_tiles;
-          const int sb = n % NBUF, s = n % NSTAGE;
-          const uint32_t base = tmem + sb * C::NSC * BM;
-          // barriers of tile n+1's score products, probed while this iteration issues
-          const bool nxt = n + 1 < n_tiles;
-          const uint64_t* bl = nxt ? l_full + (n + 1) % NSTAGE : done;
-          const uint32_t pl = nxt ? ((n + 1) / NSTAGE) & 1 : 0u;
-          const bool need_s = nxt && n + 1 >= NBUF;
-          const uint64_t* bs = need_s ? s_free + (n + 1) % NBUF : done;
-          const uint32_t ps = need_s ? (((n + 1) / NBUF) - 1) & 1 : 0u;
-          const uint64_t* be = n >= 1 ? e_full + ((n - 1) & 1) : done;
-          const uint32_t pe = n >= 1 ? ((n - 1) >> 1) & 1 : 0u;
-          bool next_l = false, next_s = false, seen_e = false;
-          if (has_scores) {
-            if (!have_l && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
-            if (n >= NBUF && !have_s && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
+          const int s = n % NSTAGE;
+          if (me == 0) {
+            // S^T | K u_q^T, then G_dS^T += u_k Q^T, once the elementwise warps read tile n-1
+            if (n == n_tiles) break;
+            if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (n >= 1 && !(ok = mbar_wait(s_free, (n - 1) & 1, g, 3))) break;
             tc_fence_after();
-            if constexpr (!C::E_OVERLAP) scores_e_cols(base, s, done, 0u, done, 0u);
-            const uint32_t seen = scores_free_cols(base, s, be, pe, bl, pl);
-            if constexpr (!C::E_OVERLAP) umma_commit(s_full + sb);
-            seen_e = seen & 1;
-            next_l = (seen >> 1) & 1;
+            scores_e_cols(tmem, s, done, 0u, done, 0u);
+            umma_commit(s_full);
+            umma_commit(l_empty + s);
+            continue;
           }
           if (n >= 1) {
-            // accumulate products of tile n-1
-            if (!seen_e && !(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
+            // the accumulate products of tile n-1 read its E, written over this issuer's score columns
+            if (!(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
             tc_fence_after();
-            const uint32_t seen = acc_products(n - 1, bl, pl, bs, ps);
-            if constexpr (C::E_DEDICATED) umma_commit(e_empty);
-            umma_commit(l_empty + (n - 1) % NSTAGE);
-            next_l = next_l || (seen & 1);
-            next_s = (seen >> 1) & 1;
-          }
-          if constexpr (C::E_OVERLAP) {
-            if (has_scores) {
-              // overwrites the columns of E(n-1), which the products just issued read first
-              // (tile n+1 also needs s_free(n), which cannot be complete before these scores are)
-              const uint32_t seen = scores_e_cols(base, s, bl, pl, done, 0u);
-              umma_commit(s_full + sb);
-              next_l = next_l || (seen & 1);
-              next_s = next_s || ((seen >> 1) & 1);
+            const int sp = (n - 1) % NSTAGE;
+            const uint32_t bQ = smem_u32(st0(sp)), bDO = smem_u32(st1(sp)), bUQ = bQ + BM * 128;
+            const uint32_t acc_first = n > 1 ? 1u : 0u;
+#pragma unroll
+            for (int kk = 0; kk < BM / 16; ++kk) {
+              const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
+              if (me == 1) {
+                // dd_K += dS^T u_q + G_S^T Q
+                umma_ts(tAcc0, e_col(0, kk, n - 1), desc_mnmajor(bUQ, SR0, kk), id_acc, a);
+                umma_ts(tAcc0, e_col(1, kk, n - 1), desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
+              } else {
+                // dd_V += G_dP^T dO
+                umma_ts(tAcc1, e_col(2, kk, n - 1), desc_mnmajor(bDO, BM, kk), id_acc, a);
+              }
             }
+            umma_commit(l_empty + sp);
           }
-          have_l = next_l;
-          have_s = next_s;
+          if (n < n_tiles) {
+            // dP^T = V dO^T (issuer 1) or (dO u_v^T)^T = u_v dO^T (issuer 2) over the E just read
+            if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            tc_fence_after();
+            const uint32_t b1 = smem_u32(st1(s)), a0 = me == 1 ? aV : aUV;
+            const uint32_t dcol = tmem + (me == 1 ? C::C_DP : C::C_UV);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_ss(dcol, desc_kmajor(a0, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
+            umma_commit(s_full);
+          }
         }
-        if (ok) umma_commit(acc_full);
-        umma_commit(drain);
-        mbar_drain(drain, 0);
+        if (me != 0 && ok) umma_commit(acc_full);
+        umma_commit(drain + me);
+        mbar_drain(drain + me, 0);
       }
     }
    }
@@ -545,7 +563,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           if constexpr (C::E_DEDICATED) return tE + lane_off + (c0 >> 1) + j * C::E_COLS;
           const uint32_t off = 32 * half + (j == 2 ? BM : 16 * j);
           if constexpr (C::E_OWN) return tmem + lane_off + sb * C::NSC * BM + off;
-          return tmem + lane_off + off;
+          return tE + lane_off + off;
         };
         uint32_t w[16];
 #pragma unroll
