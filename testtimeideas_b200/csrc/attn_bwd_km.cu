@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       mbar_init(acc_full, 2);
     }
     if (C::THREE_ISSUERS) {  // all three read a stage and write score columns
-      mbar_init(s_full, 3);
+      mbar_init(s_full + 1, 2);  // s_full[0]: S^T, G_dS^T (issuer 0); s_full[1]: dP^T, (dO u_v^T)^T
       for (int i = 0; i < 4; ++i) mbar_init(l_empty + i, 3);
       mbar_init(acc_full, 2);  // issuers 1 and 2
     }
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
               umma_ss(dcol, desc_kmajor(a0, BK, kk), desc_kmajor(b1, BM, kk), id_n1, kk > 0);
-            umma_commit(s_full);
+            umma_commit(s_full + 1);
           }
         }
         if (me != 0 && ok) umma_commit(acc_full);
@@ -477,6 +477,97 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       const int sb = n % NBUF, s = n % NSTAGE;
       const int qt = qt0 + n;
       const int qcol0 = qt * BM + c0;
+      if constexpr (C::THREE_ISSUERS) {
+        // Two phases: S^T and G_dS^T come from issuer 0 well before dP^T and
+        // (dO u_v^T)^T, which follow the previous tile's accumulate products;
+        // P^T, G_dP^T and E tile 2 are formed while those run.
+        if (!mbar_wait(s_full + 0, n & 1, g, 6)) { ok = false; break; }
+        if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 9)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t base = tmem + lane_off + c0;
+        float sv[CPW], gd[CPW];
+        tmem_ld_nw<CPW>(base + C::C_S, sv);
+        tmem_ld_nw<CPW>(base + C::C_GDS, gd);
+        tmem_wait_ld();
+        reg_fence(sv);
+        reg_fence(gd);
+        tc_fence_before();
+        mbar_arrive(s_free);  // issuer 0 may compute the next tile's S^T, G_dS^T
+        const bool need_mask = key_edge || (CAUSAL && (qt * BM < k0 + BK - 1 || qt * BM + BM - 1 > band_last));
+        const float4* st_lse = reinterpret_cast<const float4*>(statS(s, 0) + c0);
+        const float4* st_del = reinterpret_cast<const float4*>(statS(s, 1) + c0);
+        const float4* st_gam = reinterpret_cast<const float4*>(statS(s, 2) + c0);
+        const float4* st_rho = reinterpret_cast<const float4*>(statS(s, 3) + c0);
+        uint32_t e2[CPW / 2];  // packed G_dP^T (E tile 2)
+        auto phase_a = [&](auto masked) {
+#pragma unroll
+          for (int q4 = 0; q4 < CPW / 4; ++q4) {
+            const float4 l4 = st_lse[q4], g4 = st_gam[q4];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int e = q4 * 4 + h2 * 2;
+              float x0, x1;
+              split(sub2(mul2(f2(sv[e], sv[e + 1]), C2), h2 ? f2(l4.z, l4.w) : f2(l4.x, l4.y)), x0, x1);
+              float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+              if (static_cast<bool>(masked)) {
+                const int qi = qcol0 + e;
+                p0 = ((key < T) && (!CAUSAL || (key <= qi && qi <= key_hi))) ? p0 : 0.f;
+                p1 = ((key < T) && (!CAUSAL || (key <= qi + 1 && qi + 1 <= key_hi))) ? p1 : 0.f;
+              }
+              const F2 PR = f2(p0, p1);
+              const F2 GDS = mul2(f2(gd[e], gd[e + 1]), SC2);
+              float g0, g1;
+              split(mul2(PR, sub2(GDS, h2 ? f2(g4.z, g4.w) : f2(g4.x, g4.y))), g0, g1);  // G_dP^T
+              e2[e >> 1] = pack2<BF16>(g0, g1);
+              sv[e] = p0;
+              sv[e + 1] = p1;
+              split(GDS, gd[e], gd[e + 1]);
+            }
+          }
+        };
+        if constexpr (CAUSAL) {
+          if (need_mask) phase_a(std::true_type{});
+          else phase_a(std::false_type{});
+        } else {
+          phase_a(need_mask);
+        }
+        if (!mbar_wait(s_full + 1, n & 1, g, 10)) { ok = false; break; }
+        tc_fence_after();
+        float dp[CPW], uv[CPW];
+        tmem_ld_nw<CPW>(base + C::C_DP, dp);
+        tmem_ld_nw<CPW>(base + C::C_UV, uv);
+        tmem_wait_ld();
+        reg_fence(dp);
+        reg_fence(uv);
+#pragma unroll
+        for (int q4 = 0; q4 < CPW / 4; ++q4) {
+          const float4 d4 = st_del[q4], g4 = st_gam[q4], r4 = st_rho[q4];
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int e = q4 * 4 + h2 * 2;
+            const F2 PR = f2(sv[e], sv[e + 1]), DP = f2(dp[e], dp[e + 1]), GDS = f2(gd[e], gd[e + 1]);
+            const F2 GAM = h2 ? f2(g4.z, g4.w) : f2(g4.x, g4.y);
+            const F2 RHO = h2 ? f2(r4.z, r4.w) : f2(r4.x, r4.y);
+            const F2 DPM = sub2(DP, h2 ? f2(d4.z, d4.w) : f2(d4.x, d4.y));
+            const F2 GPR = fma2(GDS, DPM, sub2(f2(uv[e], uv[e + 1]), fma2(GAM, DP, RHO)));  // G_P - rho
+            split(mul2(PR, DPM), sv[e], sv[e + 1]);  // dS^T
+            split(mul2(PR, GPR), dp[e], dp[e + 1]);  // G_S^T
+          }
+        }
+        // E over the columns just read: dS^T, G_S^T over dP^T, G_dP^T over (dO u_v^T)^T
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(sv[2 * j], sv[2 * j + 1]);
+        tmem_st16_raw(tE + lane_off + 32 * half, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = pack2<BF16>(dp[2 * j], dp[2 * j + 1]);
+        tmem_st16_raw(tE + lane_off + 32 * half + 16, w);
+        tmem_st16_raw(tE + lane_off + 32 * half + BM, e2);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(e_full + (n & 1));
+        continue;
+      }
       if (!mbar_wait(s_full + sb, (n / NBUF) & 1, g, 6)) { ok = false; break; }
       // The per-query statistics arrived by TMA on l_full[s]; that phase cannot
       // advance until this tile's elementwise step is done.
