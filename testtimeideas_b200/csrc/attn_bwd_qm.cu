@@ -15,11 +15,11 @@
 //            double backward of TritonDvFn / TritonRowSumFn / TritonDqDkFn,
 //            backward_stubs.py:435-514, with the complete second-order terms)
 //
-// Roles (320 threads): warps 0..7 elementwise, warp 8 MMA issuer (one
-// thread), warp 9 TMA producer (with SPLIT_REGS, 384 threads: warps 10-11 idle
-// complete the control warpgroup, which gives registers to the elementwise
-// warpgroups with setmaxnreg). Compute warp w owns TMEM lanes 32*(w%4)..+31
-// (one query row per thread) and columns (w/4)*BN/2 .. +BN/2 of every tile.
+// Roles (352 threads): warps 0..7 elementwise, warps 8 and 10 MMA issuers
+// (one thread each: one thread issues at most one tcgen05.mma per ~85 cycles,
+// below the tensor pipe's rate), warp 9 TMA producer. Compute warp w owns TMEM
+// lanes 32*(w%4)..+31 (one query row per thread) and columns (w/4)*BN/2 ..
+// +BN/2 of every tile.
 //
 // Score products that share their A operand run as one N = 2*BN product: the
 // streamed K and u_k tiles sit stacked in one panel ([K; u_k]), as do V and
