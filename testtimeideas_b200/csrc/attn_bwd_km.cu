@@ -110,6 +110,11 @@ struct KmCfg {
   // a tile) against issuer 0's 8 for S^T, so issuer 0 also takes dV += P^T dO;
   // a stage is then released by both (l_empty and acc_full count two commits).
   static constexpr bool ACC_SPLIT = SPLIT_SCORES && !BWD2;
+  // With ACC_SPLIT, dS^T (read by issuer 1's dK products) lies over the dP^T
+  // columns that issuer 1 overwrites next, P^T (issuer 0's dV) over S^T: each
+  // issuer overwrites only E that it has read itself, so no completion wait
+  // (e_cons) crosses the two issuers.
+  static constexpr bool E1_OVER_DP = ACC_SPLIT;
   static constexpr int NTHREADS =
       NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0) + (THREE_ISSUERS ? 64 : 0);
   static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : (E_OVERLAP ? 2 * BM : 0);
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   // take tile 2 (first order: S^T; double backward: dP^T, then (dO u_v^T)^T).
   auto e_col = [&](int j, int kk, int n) -> uint32_t {
     if constexpr (C::E_DEDICATED) return tE + j * C::E_COLS + kk * 8;
-    const uint32_t off = 32 * (kk >> 1) + (kk & 1) * 8 + (j == 2 ? BM : 16 * j);
+    const uint32_t off = 32 * (kk >> 1) + (kk & 1) * 8 + (C::E1_OVER_DP ? j * C::C_DP : (j == 2 ? BM : 16 * j));
     if constexpr (C::E_OWN) return tmem + (n % NBUF) * C::NSC * BM + off;
     return tE + off;
   };
@@ -380,7 +385,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
             if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
             // E over its own score buffer: the accumulate products that read it completed
-            if (me == 0 && C::E_OWN && n >= NBUF && !(ok = mbar_wait(e_cons + sb, ((n / NBUF) - 1) & 1, g, 5)))
+            if (me == 0 && C::E_OWN && !C::E1_OVER_DP && n >= NBUF &&
+                !(ok = mbar_wait(e_cons + sb, ((n / NBUF) - 1) & 1, g, 5)))
               break;
             tc_fence_after();
             if (me == 0) scores_e_cols(base, s, done, 0u, done, 0u);
@@ -393,7 +399,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             acc_products(n - 1, done, 0u, done, 0u, C::ACC_SPLIT ? (me == 0 ? 1 : 2) : 3);
             if constexpr (C::E_DEDICATED) umma_commit(e_empty);
             // issuer 0's own score products into this buffer follow its dV products in order
-            if constexpr (C::E_OWN) {
+            if constexpr (C::E_OWN && !C::E1_OVER_DP) {
               if (me == 1) umma_commit(e_cons + (n - 1) % NBUF);
             }
             umma_commit(l_empty + (n - 1) % NSTAGE);
@@ -652,7 +658,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         // this thread's 16 words of E tile j (see e_col)
         auto e_put = [&](int j) -> uint32_t {
           if constexpr (C::E_DEDICATED) return tE + lane_off + (c0 >> 1) + j * C::E_COLS;
-          const uint32_t off = 32 * half + (j == 2 ? BM : 16 * j);
+          const uint32_t off = 32 * half + (C::E1_OVER_DP ? j * C::C_DP : (j == 2 ? BM : 16 * j));
           if constexpr (C::E_OWN) return tmem + lane_off + sb * C::NSC * BM + off;
           return tE + lane_off + off;
         };
