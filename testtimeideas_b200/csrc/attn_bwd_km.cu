@@ -104,11 +104,13 @@ struct KmCfg {
   static constexpr bool TWO_ISSUERS = !E_OVERLAP;
   // Split the score products too: issuer 0 those over the columns E may use
   // (S^T, G_dS^T), issuer 1 the others (dP^T, (dO u_v^T)^T) and the accumulates.
-  // Measured: 8% faster for the d=128 backward, no gain or a loss at d=64.
-  static constexpr bool SPLIT_SCORES = TWO_ISSUERS && D == 128;
-  // First-order d=128: issuer 1 would issue dP^T and both accumulates (16 UMMAs
-  // a tile) against issuer 0's 8 for S^T, so issuer 0 also takes dV += P^T dO;
-  // a stage is then released by both (l_empty and acc_full count two commits).
+  // Measured: 8% faster for the d=128 backward, no gain or a loss for the d=64
+  // double backward.
+  static constexpr bool SPLIT_SCORES = TWO_ISSUERS && (D == 128 || !BWD2);
+  // First order: issuer 1 would issue dP^T and both accumulates (16 UMMAs a
+  // tile at d=128) against issuer 0's 8 for S^T, so issuer 0 also takes dV +=
+  // P^T dO; a stage is then released by both (l_empty and acc_full count two
+  // commits).
   static constexpr bool ACC_SPLIT = SPLIT_SCORES && !BWD2;
   // With ACC_SPLIT, dS^T (read by issuer 1's dK products) lies over the dP^T
   // columns that issuer 1 overwrites next, P^T (issuer 0's dV) over S^T: each
