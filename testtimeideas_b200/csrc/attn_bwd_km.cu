@@ -21,9 +21,11 @@
 //
 // The elementwise results E (16-bit P^T, dS^T | dS^T, G_S^T, G_dP^T) live in
 // TMEM as packed pairs and are the A operand of the accumulate products:
-//   kBwdKV: over the S^T columns of the tile's own score buffer (two
-//     buffers), each thread writing only the columns it read (its half's 32
-//     S^T columns take its 16 P^T and 16 dS^T words);
+//   kBwdKV: over the tile's own score buffer (two buffers), each thread
+//     writing only columns it read: its 16 P^T words over its half's S^T
+//     columns (read by issuer 0's dV products, before issuer 0's next S^T
+//     product there), its 16 dS^T words over its half's dP^T columns (issuer
+//     1's dK products, then issuer 1's next dP^T);
 //   kBwd2KV d=64: a dedicated region;
 //   kBwd2KV d=128, where four 64-wide score tiles and two 128-wide
 //     accumulators fill all 512 columns: dS^T and G_S^T over the dP^T columns,
