@@ -96,6 +96,18 @@ CONFIGS = {
                 workload="streaming inference of the reference's latency demo: 8 layers d_model=512 8 heads "
                          "d_ff=2048 vocab 4096 window 512, bf16 (the demo's fp32 model cast: the kernels take "
                          "16-bit), 8192 tokens in chunks of 512, each forward over the last 512 tokens"),
+    # BASELINE config 3 as the reference's own sweep runs it (tests/bench_gradgrad_sweep.py:76):
+    # T in {512 ... 16384} x causal / non-causal, mode save_p_triton_full; one JSON line with a row per case
+    "c3sweep": dict(b=1, h=1, t=16384, d=64, dtype="fp16", causal=True, scale_in=1.0, step="c3sweep",
+                    ts=(512, 1024, 2048, 4096, 8192, 16384),
+                    workload="BASELINE config 3: grad-grad sweep b=1 h=1 d=64 fp16, T in {512..16384}, causal and "
+                             "non-causal, mode save_p_triton_full"),
+    # BASELINE config 2 as defined: forward + first-order backward in the modes save_p and
+    # save_p_triton_full, causal and non-causal, 50 iterations (tests/bench_gradgrad.py:54, tests/bench.py:30-38)
+    "c2modes": dict(b=2, h=4, t=2048, d=128, dtype="fp16", causal=False, scale_in=0.5, step="c2modes",
+                    modes=("save_p", "save_p_triton_full"), iters=50,
+                    workload="BASELINE config 2: fwd+bwd b=2 h=4 T=2048 d=128 fp16, modes save_p and "
+                             "save_p_triton_full, causal and non-causal, 50 iterations"),
     "c8p": dict(b=1, h=8, t=8192, d=128, dtype="fp16", causal=False, scale_in=0.5, step="from_p",
                 workload="fwd (P written) + first-order backward from P, b=1 h=8 T=8192 d=128 fp16 "
                          "non-causal (P = 1 GiB, larger than L2)"),
@@ -114,8 +126,8 @@ def causal_factor(t: int, causal: bool) -> float:
 
 def step_flops(cfg: dict, heads: int) -> float:
     """Algorithmic flops of one step: 28 T^2 d per head for the grad-grad step,
-    12 T^2 d for forward + first-order backward (the from-P step)."""
-    units = {"from_p": 12.0, "fwd": 4.0}.get(cfg.get("step"), 28.0)
+    12 T^2 d for forward + first-order backward (the from-P and config-2 steps)."""
+    units = {"from_p": 12.0, "fwd": 4.0, "fwdbwd": 12.0}.get(cfg.get("step"), 28.0)
     return units * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
 
 
@@ -224,6 +236,8 @@ def math_path_step(kind: str):
                 return (attention_math(x["q"], x["k"], x["v"], causal, scale),)
         q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
         o = attention_math(q, k, v, causal, scale)
+        if kind == "fwdbwd":
+            return torch.autograd.grad(o, (q, k, v), x["do"])
         if kind == "sweep":
             grads = torch.autograd.grad(o.float().mean(), (q, k, v), create_graph=True)
             return torch.autograd.grad(sum(g.float().pow(2).mean() for g in grads), (q, k, v))
@@ -238,7 +252,7 @@ def time_math_path(cfg: dict, x: dict, kind: str, steps: int, device,
     intermediates fit comfortably (about 12 of them per head in flight); with
     `flush`, L2 is flushed between steps outside the per-step events, as for ours."""
     heads = x["q"].shape[0] * x["q"].shape[1]
-    if kind not in ("gradgrad", "fwd", "sweep") or heads * cfg["t"] ** 2 * 2 * 12 > 48 * 2 ** 30:
+    if kind not in ("gradgrad", "fwd", "sweep", "fwdbwd") or heads * cfg["t"] ** 2 * 2 * 12 > 48 * 2 ** 30:
         return None
     step = math_path_step(kind)
     try:
@@ -296,13 +310,90 @@ def sweep_step(x: dict, causal: bool):
     return torch.autograd.grad(sum(g.float().pow(2).mean() for g in grads), (q, k, v))
 
 
-def gradgrad_step(x: dict, causal: bool):
+def gradgrad_step(x: dict, causal: bool, mode: str = "recompute"):
     """One step through the public, reference-compatible API."""
     from ttt_kernels import triton_attention
     q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
-    o = triton_attention(q, k, v, causal=causal)
+    o = triton_attention(q, k, v, causal=causal, bwd_mode=mode)
     dq, dk, dv = torch.autograd.grad(o, (q, k, v), x["do"], create_graph=True)
     return torch.autograd.grad((dq, dk, dv), (q, k, v), (x["uq"], x["uk"], x["uv"]))
+
+
+def fwd_bwd_step(mode: str):
+    """Forward + first-order backward (no graph kept) through the public API in
+    bwd_mode `mode`: the step BASELINE config 2 times per mode."""
+    def step(x: dict, causal: bool):
+        from ttt_kernels import triton_attention
+        q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+        o = triton_attention(q, k, v, causal=causal, bwd_mode=mode)
+        return torch.autograd.grad(o, (q, k, v), x["do"])
+    return step
+
+
+# ---------------------------------------------------------------- timing helpers
+def timed_ms(step, x: dict, causal: bool, steps: int, flush: Optional[torch.Tensor] = None) -> float:
+    """Total CUDA-event milliseconds of `steps` steps on the current stream. With
+    `flush`, a 512 MiB write before each step flushes L2, outside that step's events."""
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step(x, causal)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+    evs = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step(x, causal)
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def profiled_kernels(step, x: dict, causal: bool, steps: int, flush: Optional[torch.Tensor] = None) -> dict:
+    """{kernel kind: (launches, total ms)} over `steps` steps with the library's profiling
+    hook on (each launch bracketed by CUDA events on its stream)."""
+    from testtimeideas_b200 import _lib
+    torch.cuda.synchronize()
+    _lib.profile_collect()
+    _lib.profile_enable(True)
+    for _ in range(steps):
+        if flush is not None:
+            flush.fill_(1)
+        step(x, causal)
+    torch.cuda.synchronize()
+    _lib.profile_enable(False)
+    return {k: v for k, v in _lib.profile_collect().items() if v[0] > 0}
+
+
+def soak(step, x: dict, causal: bool, seconds: float, flush: Optional[torch.Tensor] = None) -> dict:
+    """Untimed steps, one at a time, until `seconds` have passed: the GPU reaches the
+    clocks of sustained load (the power cap) before the timed region starts, so timed
+    regions of any length (a 4 s region at one GPU, a 0.6 s one at eight) see the
+    same clock state."""
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds:
+        if flush is not None:
+            flush.fill_(1)
+        step(x, causal)
+        torch.cuda.synchronize()
+        n += 1
+    return {"steps": n, "seconds": round(time.perf_counter() - t0, 2)}
+
+
+def fused_bwd_summary(kernel_ms: dict, cfg: dict, heads: int, peak: float) -> dict:
+    """The first-order backward (delta + dK/dV + dQ passes) per step: its algorithmic
+    8 T^2 d per head over its kernels' time, against the sustained tensor peak."""
+    ms = sum(kernel_ms.get(k, 0.0) for k in ("delta", "bwd_kv", "bwd_q"))
+    flops = 8.0 * cfg["t"] ** 2 * cfg["d"] * heads * causal_factor(cfg["t"], cfg["causal"])
+    tflops = flops / (ms * 1e-3) / 1e12 if ms > 0 else None
+    return {"ms_per_step": ms, "algorithmic_tflops": tflops, "frac_of_sustained_peak": tflops / peak if tflops else None,
+            "kernels": ["delta", "bwd_kv", "bwd_q"], "target_frac": 0.5}
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
@@ -514,6 +605,127 @@ def run_stream(args, cfg: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
+def north_star(device: torch.device, peaks: dict, peak_src: str, steps: int = 20) -> dict:
+    """BASELINE config 3 at its largest T, the north_star's target configuration: b=h=1
+    T=16384 d=64 fp16 causal on one GPU, in the reference sweep's mode
+    (save_p_triton_full). Ours (CUDA events, L2 flushed between steps); the reference's
+    math formulation (torch matmul/softmax, autograd twice) on the same GPU and inputs
+    with the speed-up over it (target >= 2x); and the first-order backward's
+    algorithmic fraction of the sustained tensor peak (target >= 0.5)."""
+    cfg = CONFIGS["c3"]
+    x = make_inputs(cfg, range(1), device)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    step = lambda x_, c_: gradgrad_step(x_, c_, "save_p_triton_full")  # noqa: E731
+    for _ in range(5):
+        flush.fill_(1)
+        step(x, True)
+    ms = timed_ms(step, x, True, steps, flush) / steps
+    prof = profiled_kernels(step, x, True, steps, flush)
+    kernel_ms = {k: v[1] / steps for k, v in prof.items()}
+    sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    math_path = time_math_path(cfg, x, "gradgrad", 10, device, flush)
+    out = {"workload": "BASELINE config 3 at T=16384: grad-grad b=1 h=1 d=64 fp16 causal, mode save_p_triton_full, "
+                       "one GPU, L2 flushed between steps",
+           "ms_per_step": ms, "algorithmic_tflops": step_flops(cfg, 1) / (ms * 1e-3) / 1e12, "steps": steps,
+           "kernel_ms_per_step": kernel_ms,
+           "fused_bwd": dict(fused_bwd_summary(kernel_ms, cfg, 1, sustained),
+                             peak=sustained, peak_source=f"{peak_src} bf16_tflops_sustained"),
+           "math_path_gpu": math_path, "target_speedup_vs_math_path": 2.0}
+    if math_path and "ms_per_step" in math_path:
+        out["speedup_vs_math_path"] = math_path["ms_per_step"] / ms
+    return out
+
+
+def run_sweep(args, cfg: dict) -> None:
+    """Config 3 over the reference sweep's sequence lengths (tests/bench_gradgrad_sweep.py:76),
+    causal and non-causal, mode save_p_triton_full, one GPU: per case ours and the math path on
+    the same GPU, each in the probe form (28 T^2 d) and in the sweep's loss form (mean(O),
+    sum mean(g^2)); L2 flushed between steps. Prints one JSON line with a row per case."""
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("the sweep runs on one GPU")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peaks, peak_src = load_peaks()
+    sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    steps = max(args.steps, 10)
+    rows = []
+    clocks = ClockSampler(0)
+    probe = lambda x_, c_: gradgrad_step(x_, c_, "save_p_triton_full")  # noqa: E731
+    for causal in (False, True):
+        for t in cfg["ts"]:
+            c = dict(cfg, t=t, causal=causal, step=None)
+            x = make_inputs(c, range(1), device)
+            row = {"t": t, "causal": causal}
+            for form, fn in (("probe", probe), ("loss", sweep_step)):
+                for _ in range(args.warmup):
+                    flush.fill_(1)
+                    fn(x, causal)
+                ms = timed_ms(fn, x, causal, steps, flush) / steps
+                row[f"{form}_ms"] = ms
+                mp = time_math_path(c, x, "gradgrad" if form == "probe" else "sweep", min(steps, 10), device, flush)
+                if mp and "ms_per_step" in mp:
+                    row[f"{form}_math_path_ms"] = mp["ms_per_step"]
+                    row[f"{form}_speedup_vs_math_path"] = mp["ms_per_step"] / ms
+            row["algorithmic_tflops"] = step_flops(c, 1) / (row["probe_ms"] * 1e-3) / 1e12
+            row["frac_of_sustained_peak"] = row["algorithmic_tflops"] / sustained
+            rows.append(row)
+    clk = clocks.stop()
+    big = [r for r in rows if r["t"] == max(cfg["ts"]) and r["causal"]][0]
+    line = {"metric": METRIC, "value": big["algorithmic_tflops"], "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": big["probe_ms"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+            "config": {"workload": cfg["workload"], "value_row": "T=16384 causal, probe form",
+                       "l2": "L2 flushed (512 MiB write) between timed steps"},
+            "peak": sustained, "peak_source": f"{peak_src} bf16_tflops_sustained", "rows": rows, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+def run_c2modes(args, cfg: dict) -> None:
+    """Config 2 as BASELINE defines it: forward + first-order backward through the public API
+    in the modes save_p and save_p_triton_full, causal and non-causal, 50 timed iterations
+    each (tests/bench_gradgrad.py:54 modes; the shape of tests/bench.py:30-38), with the math
+    path on the same GPU; L2 flushed between steps. One JSON line with a row per case."""
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("config 2 runs on one GPU")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    iters = cfg["iters"]
+    heads = cfg["b"] * cfg["h"]
+    rows = []
+    clocks = ClockSampler(0)
+    for causal in (False, True):
+        c = dict(cfg, causal=causal, step="fwdbwd")
+        x = {n: v.reshape(cfg["b"], cfg["h"], cfg["t"], cfg["d"])
+             for n, v in make_inputs(c, range(heads), device).items() if n in ("q", "k", "v", "do")}
+        mp = time_math_path(c, x, "fwdbwd", iters, device, flush)
+        for mode in cfg["modes"]:
+            step = fwd_bwd_step(mode)
+            for _ in range(max(args.warmup, 10)):
+                flush.fill_(1)
+                step(x, causal)
+            ms = timed_ms(step, x, causal, iters, flush) / iters
+            prof = profiled_kernels(step, x, causal, iters, flush)
+            row = {"mode": mode, "causal": causal, "ms": ms,
+                   "algorithmic_tflops": step_flops(c, heads) / (ms * 1e-3) / 1e12,
+                   "kernel_ms_per_step": {k: v[1] / iters for k, v in prof.items()}}
+            if mp and "ms_per_step" in mp:
+                row["math_path_ms"] = mp["ms_per_step"]
+                row["speedup_vs_math_path"] = mp["ms_per_step"] / ms
+            rows.append(row)
+    clk = clocks.stop()
+    first = rows[0]
+    line = {"metric": "fwd+bwd attention step ms & TFLOP/s (BASELINE config 2)", "value": first["algorithmic_tflops"],
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": iters, "warmup": max(args.warmup, 10),
+            "ms_per_step": first["ms"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": cfg["dtype"], "data": "synthetic",
+            "config": {"workload": cfg["workload"], "value_row": "save_p non-causal",
+                       "l2": "L2 flushed (512 MiB write) between timed steps"},
+            "rows": rows, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, cfg: dict) -> None:
     from testtimeideas_b200 import _lib
     from testtimeideas_b200.sharding import head_range, max_over_ranks as _max_over_ranks
@@ -563,6 +775,9 @@ def run_ours(args, cfg: dict) -> None:
             flush.fill_(1)
         step(x, cfg["causal"])
     _lib.check_device_errors(device)
+    # then untimed steps until the clocks settle under sustained load, so that every N's
+    # timed region (4 s at one GPU, under a second at eight) starts in the same state
+    soaked = soak(step, x, cfg["causal"], args.soak_s, flush) if args.soak_s > 0 else {"steps": 0, "seconds": 0.0}
 
     # ---- device-timed region: inputs resident in HBM. Timed without the profiling
     # hook (with it on, the library keeps every launch on one stream so that each
@@ -618,7 +833,7 @@ def run_ours(args, cfg: dict) -> None:
     # independent), so that one chunk's host-to-device copy, another's compute and a
     # third's device-to-host copy overlap on three streams; every step still copies
     # all of its inputs in and all of its results out.
-    nchunk = max(1, min(8, heads // 8))
+    nchunk = min(8, heads) if heads >= 8 else 1
     bounds = [round(i * heads / nchunk) for i in range(nchunk + 1)]
     comp = torch.cuda.current_stream(device)
     copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -652,6 +867,29 @@ def run_ours(args, cfg: dict) -> None:
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
     e2e_value = step_flops(cfg, total_heads) / (e2e_ms * 1e-3) / 1e12
+    # The ceiling the copies alone set: the same pinned copies, in and out on their two
+    # streams, with no compute, on every rank at once (the ranks share the host).
+    out_dev = [torch.empty_like(x["q"]) for _ in host_out]
+    barrier()
+    torch.cuda.synchronize(device)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(c0)
+            for n in dev_in:
+                dev_in[n].copy_(host_in[n], non_blocking=True)
+        with torch.cuda.stream(copy_out):
+            copy_out.wait_event(c0)
+            for dst, src in zip(host_out, out_dev):
+                dst.copy_(src, non_blocking=True)
+    comp.wait_stream(copy_in)
+    comp.wait_stream(copy_out)
+    c1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    copy_ms = max_over_ranks(c0.elapsed_time(c1)) / e2e_steps
+    del out_dev
 
     # ---- roofline of the dominant kernel (per-launch CUDA-event time inside the timed region)
     peaks, peak_src = load_peaks()
@@ -698,6 +936,10 @@ def run_ours(args, cfg: dict) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, args.cpu_t, reps=1)
 
+    ns = None
+    if world == 1 and args.config == "c4" and not args.no_north_star:
+        ns = north_star(device, peaks, peak_src)
+
     if rank == 0:
         dtype = cfg["dtype"]
         line = {
@@ -714,13 +956,22 @@ def run_ours(args, cfg: dict) -> None:
                                   ", plus P" if kind == "from_p" else ""))},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms, "steps": e2e_steps,
                     "head_chunks": nchunk,
-                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "copy_only_ms_per_step": copy_ms,
+                    "copy_only_gbs_per_gpu": (h2d + d2h) / (copy_ms * 1e-3) / 1e9,
+                    "ceiling_ms_per_step": max(ms_per_step, copy_ms)},
+            "soak": soaked,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": gpu_launches,
             "kernel_ms_per_step": kernel_ms,
         }
+        if kind == "gradgrad":
+            sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+            line["fused_bwd"] = dict(fused_bwd_summary(kernel_ms, cfg, heads, sustained), per="rank 0, per GPU")
+        if ns is not None:
+            line["north_star"] = ns
         if verify is not None:
             line["verify"] = verify
         if math_path is not None:
@@ -743,6 +994,11 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-math-path", action="store_true",
                     help="skip timing the reference's math formulation on the GPU beside the kernels")
+    ap.add_argument("--no-north-star", action="store_true",
+                    help="skip the config-3 north-star measurement appended to the default (config 4) line")
+    ap.add_argument("--soak-s", type=float, default=4.0,
+                    help="seconds of untimed steps after the warm-up, so that the timed region starts with the "
+                         "clocks of sustained load")
     ap.add_argument("--verify", action="store_true",
                     help="gather the last step's grad-grads to rank 0 and check them against rank 0 running "
                          "every head alone (untimed)")
@@ -756,6 +1012,10 @@ def main() -> None:
         run_meta(args, cfg)
     elif cfg.get("step") == "stream":
         run_stream(args, cfg)
+    elif cfg.get("step") == "c3sweep":
+        run_sweep(args, cfg)
+    elif cfg.get("step") == "c2modes":
+        run_c2modes(args, cfg)
     else:
         run_ours(args, cfg)
 

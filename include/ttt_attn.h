@@ -28,8 +28,11 @@
  *    stream); no entry point synchronizes the host.
  *  - Return value: TTT_OK or a ttt_status code. Argument errors are detected
  *    on the host before anything is enqueued. `err` (optional, device int32)
- *    receives a nonzero code if a kernel gave up on a bounded wait; the
- *    caller reads it after synchronizing.
+ *    receives a nonzero code if a kernel gave up on a bounded wait
+ *    (TTT_ERR_WORD_TIMEOUT | site << 8 | block bits); the caller reads it
+ *    after synchronizing, or polls a registered host mirror
+ *    (ttt_attn_error_mirror). While it is nonzero, kernels given that word
+ *    exit at once: the caller clears it (in stream order) to go on.
  *
  * Reference interface each entry point replaces (paths inside
  * ry2009/TestTimeIdeas) is cited on the declaration.
@@ -58,7 +61,8 @@ enum ttt_status {
   TTT_ERR_DRIVER = 9,      /* the driver entry point for tensor maps is unavailable */
   TTT_ERR_UNSUPPORTED = 10, /* valid request this build does not implement */
   TTT_ERR_SCRATCH = 11,     /* b*h*t_pad exceeds TTT_ATTN_NOALLOC_MAX_ROWS (ttt_attn_bwd2_noalloc) */
-  TTT_ERR_SCRATCH_SETUP = 12 /* the built-in scratch array's device address could not be obtained */
+  TTT_ERR_SCRATCH_SETUP = 12, /* the built-in scratch array's device address could not be obtained */
+  TTT_ERR_MIRROR = 13         /* ttt_attn_error_mirror: not pinned host memory mapped at the same address */
 };
 
 enum ttt_dtype { TTT_F16 = 0, TTT_BF16 = 1 };
@@ -206,10 +210,33 @@ int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds);
  * b*h*t_pad <= TTT_ATTN_NOALLOC_MAX_ROWS, else returns TTT_ERR_SCRATCH before
  * enqueuing anything. All calls on a device share the array: calls that
  * overlap on the GPU race. The first call on a device looks up the array's
- * device address (with that device current) and should come before any stream
- * capture. */
+ * device address (with that device current; cached per CUDA context, so a
+ * device reset or another context gets its own lookup) and should come before
+ * any stream capture. Under lazy module loading (CUDA's default since 12.2)
+ * that first call is also when the driver loads the module holding the array
+ * and allocates it: callers that may not allocate during execution make one
+ * warm-up call per device during set-up, or run with CUDA_MODULE_LOADING=EAGER. */
 #define TTT_ATTN_NOALLOC_MAX_ROWS (1 << 20)
 int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream);
+
+/* Failure reporting without a host synchronization (no reference counterpart:
+ * the reference's Triton kernels have no bounded waits). host_word must be
+ * pinned host memory (cudaHostAlloc / cudaMallocHost) that the device sees at
+ * the same address (unified addressing), 4-byte aligned; it is registered for
+ * the CUDA context current on the calling thread (NULL unregisters). From then
+ * on, a kernel of that context that reports an error into a pass's `err` word
+ * also stores the same code into host_word, on the error path only, so the
+ * host can poll it, e.g. at the entry of its next call. The library never
+ * clears it; the caller does. */
+int ttt_attn_error_mirror(int32_t* host_word);
+
+/* Test hook for the failure path (no reference counterpart): one kernel runs the
+ * library's bounded mbarrier wait on a barrier that nothing completes, with a
+ * limit of limit_ns (1 .. 1e10). No TMA or tensor-core work is in flight; when
+ * the limit passes, the kernel records TTT_ERR_WORD_TIMEOUT | (0xfe << 8) in *err
+ * (device int32) and in the registered mirror, and returns. */
+#define TTT_ERR_WORD_TIMEOUT 0x40000000
+int ttt_attn_selftest_wait(int64_t limit_ns, int32_t* err, void* stream);
 
 /* roundup(t, 128): the row count of every statistics array. */
 int ttt_attn_t_pad(int t);

@@ -1,7 +1,7 @@
 """Generate the golden vectors in tests/golden/ from the reference itself.
 
-Runs only where the reference checkout exists (default /root/reference, or
-$TTT_REFERENCE_DIR). It imports the reference's ``ttt_kernels`` package under
+Runs only where a reference checkout exists: pass its directory with
+--reference DIR or in $TTT_REFERENCE_DIR. It imports the reference's ``ttt_kernels`` package under
 the alias ``ref_ttt_kernels`` (its own name is taken by the drop-in package of
 this repository) and calls its public entry point
 ``triton_attention(q, k, v, causal=..., bwd_mode=...)`` on CPU tensors, where
@@ -18,7 +18,7 @@ reference's ``save_p`` mode on the same inputs as the math path; its
 grad-grad for q and k differs from the math path because P is saved as a
 constant (backward_stubs.py:428-514); the tests pin that difference too.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <checkout of ry2009/TestTimeIdeas>
 """
 
 from __future__ import annotations
@@ -33,7 +33,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TTT_REFERENCE_DIR", "/root/reference"))
+REF = Path(os.environ.get("TTT_REFERENCE_DIR", "")) if os.environ.get("TTT_REFERENCE_DIR") else None
 
 # (name, b, h, t, d, causal, dtype, seed, input scale)
 CASES = [
@@ -250,6 +250,15 @@ def ttt_e2e_infer_cases(out_path: Path) -> None:
 
 
 def main() -> None:
+    import argparse
+    global REF
+    ap = argparse.ArgumentParser(description="regenerate tests/golden/*.npz from a reference checkout")
+    ap.add_argument("--reference", type=Path, default=REF,
+                    help="directory of the ry2009/TestTimeIdeas checkout (default: $TTT_REFERENCE_DIR)")
+    args = ap.parse_args()
+    if args.reference is None or not (args.reference / "ttt_kernels").is_dir():
+        raise SystemExit("give the reference checkout with --reference DIR or $TTT_REFERENCE_DIR")
+    REF = args.reference
     ttt_e2e_window_cases(HERE / "ttt_e2e_windows_fp64.npz")
     ttt_e2e_meta_cases(HERE / "ttt_e2e_meta_fp64.npz")
     ttt_e2e_infer_cases(HERE / "ttt_e2e_infer_fp64.npz")

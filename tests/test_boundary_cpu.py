@@ -249,3 +249,12 @@ def test_band_attention_wiring_matches_oracle(monkeypatch, kind):
     for name, val in (("o", out), ("dq", dq), ("gq", gq), ("gk", gk), ("gv", gv), ("gdo", gdo)):
         assert orc.normalized_err(val.detach(), ref[name]) < 1e-10, name
     assert calls == ["fwd", "bwd", "bwd2+gdo"]
+
+
+def test_failure_hooks_validate_on_the_host(lib):
+    # argument errors are caught before anything is enqueued (no GPU needed)
+    assert lib.ttt_attn_selftest_wait(1000, None, None) == 1  # TTT_ERR_NULL
+    word = ctypes.c_int32(0)
+    assert lib.ttt_attn_selftest_wait(0, ctypes.addressof(word), None) == 4  # TTT_ERR_SHAPE: limit out of range
+    assert lib.ttt_attn_selftest_wait(20_000_000_000, ctypes.addressof(word), None) == 4
+    assert b"pinned host memory" in lib.ttt_attn_status_string(13)

@@ -21,7 +21,8 @@ LIB_PATH = _PKG / "_lib" / "libttt_attn.so"
 TTT_F16, TTT_BF16 = 0, 1
 _STATUS = {
     0: "ok", 1: "null pointer", 2: "dtype", 3: "head dim", 4: "shape", 5: "stride", 6: "alignment",
-    7: "tensor map", 8: "launch", 9: "driver entry point", 10: "unsupported",
+    7: "tensor map", 8: "launch", 9: "driver entry point", 10: "unsupported", 11: "scratch", 12: "scratch setup",
+    13: "error mirror",
 }
 
 
@@ -67,7 +68,9 @@ class FromPArgs(ctypes.Structure):
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
             "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect",
             "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p", "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p",
-            "ttt_attn_work_bytes")
+            "ttt_attn_work_bytes", "ttt_attn_error_mirror", "ttt_attn_selftest_wait")
+ERR_WORD_TIMEOUT = 0x40000000  # TTT_ERR_WORD_TIMEOUT
+SELFTEST_WAIT_SITE = 0xFE
 NOALLOC_MAX_ROWS = 1 << 20  # TTT_ATTN_NOALLOC_MAX_ROWS
 KERNEL_KINDS = ("fwd", "delta", "bwd_kv", "bwd_q", "bwd2_stats", "bwd2_q", "bwd2_kv", "from_p")
 
@@ -101,6 +104,10 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         lib.ttt_attn_selftest_umma.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_void_p]
+        lib.ttt_attn_error_mirror.restype = ctypes.c_int
+        lib.ttt_attn_error_mirror.argtypes = [ctypes.c_void_p]
+        lib.ttt_attn_selftest_wait.restype = ctypes.c_int
+        lib.ttt_attn_selftest_wait.argtypes = [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         lib.ttt_attn_profile_enable.restype = ctypes.c_int
         lib.ttt_attn_profile_enable.argtypes = [ctypes.c_int]
         lib.ttt_attn_profile_collect.restype = ctypes.c_int
@@ -125,27 +132,90 @@ def t_pad(t: int) -> int:
 
 
 # ---------------------------------------------------------------- device error word
+# Per device: the int32 error word the kernels report into (device memory), and
+# a pinned host mirror of it that the library registers for the device's
+# context (ttt_attn_error_mirror). A kernel that gives up on a bounded wait
+# writes the mirror too, so every op checks it at entry without synchronizing:
+# a timeout surfaces as KernelError at the first op the host issues after the
+# failing kernel reported it (check_device_errors synchronizes and checks).
 _err_words: dict[int, torch.Tensor] = {}
+_mirrors: dict[int, tuple[torch.Tensor, ctypes.c_int32]] = {}
+
+
+def _dev_index(device: torch.device | None) -> int:
+    if device is None or device.index is None:
+        return torch.cuda.current_device()
+    return device.index
 
 
 def error_word(device: torch.device) -> torch.Tensor:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    idx = _dev_index(device)
     w = _err_words.get(idx)
     if w is None:
         w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _err_words[idx] = w
+        _register_mirror(idx)
     return w
+
+
+def _register_mirror(idx: int) -> None:
+    host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    with _on(torch.device("cuda", idx)):
+        status = load_library().ttt_attn_error_mirror(host.data_ptr())
+    if status != 0:  # the mirror is an addition: without it, errors still surface at check_device_errors
+        return
+    _mirrors[idx] = (host, ctypes.c_int32.from_address(host.data_ptr()))
+
+
+def _clear(idx: int) -> None:
+    m = _mirrors.get(idx)
+    if m is not None:
+        m[1].value = 0
+    w = _err_words.get(idx)
+    if w is not None:
+        w.zero_()
+
+
+def raise_pending(device: torch.device | None = None) -> None:
+    """Raise KernelError if a kernel on `device` has reported a failed bounded wait
+    to the host mirror; no synchronization. Clears both words (the device word in
+    stream order), so that later launches run again."""
+    idx = _dev_index(device)
+    m = _mirrors.get(idx)
+    if m is None or m[1].value == 0:
+        return
+    code = m[1].value
+    with _on(torch.device("cuda", idx)):
+        _clear(idx)
+    raise KernelError(f"libttt_attn kernel gave up on a bounded wait on cuda:{idx} (error word 0x{code:08x}); "
+                      "results of the calls since then are invalid")
 
 
 def check_device_errors(device: torch.device | None = None) -> None:
     """Synchronize and raise if any kernel on `device` gave up on a bounded wait."""
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = _dev_index(dev)
     w = error_word(dev)
     torch.cuda.synchronize(dev)
     code = int(w.item())
+    m = _mirrors.get(idx)
+    if code == 0 and m is not None:
+        code = m[1].value
     if code != 0:
-        w.zero_()
+        with _on(torch.device("cuda", idx)):
+            _clear(idx)
+            torch.cuda.synchronize(dev)
         raise KernelError(f"libttt_attn kernel timeout on {dev} (error word 0x{code:08x})")
+
+
+def selftest_wait(limit_ns: int, device: torch.device | None = None) -> None:
+    """Run the library's bounded mbarrier wait on a barrier nothing completes, with a
+    limit of `limit_ns` (test hook of the failure path). Asynchronous: the error word
+    and the host mirror receive the timeout code once the limit has passed."""
+    dev = torch.device("cuda", _dev_index(device))
+    with _on(dev):
+        w = error_word(dev)
+        _check(load_library().ttt_attn_selftest_wait(int(limit_ns), w.data_ptr(), _stream()))
 
 
 _SYNC_CHECK = os.environ.get("TTT_ATTN_SYNC_CHECK", "0") == "1"
@@ -249,6 +319,7 @@ def default_scale(d: int) -> float:
 def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: int = 0):
     """O, lse2 (fp32 [b*h, t_pad]) and, with save_p, P ([b, h, t, t])."""
     validate(q, k, v)
+    raise_pending(q.device)
     lib = load_library()
     q, k, v = prep(q), prep(k), prep(v)
     b, h, t, d = q.shape
@@ -270,6 +341,7 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: 
 def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0):
     """dq, dk, dv and delta = rowsum(dout o o) (fp32 [b*h, t_pad])."""
     validate(q, k, v)
+    raise_pending(q.device)
     lib = load_library()
     q, k, v, o, dout = prep(q), prep(k), prep(v), prep(o), prep(dout.to(q.dtype))
     b, h, t, d = q.shape
@@ -291,6 +363,7 @@ def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float
               window: int = 0):
     """Second-order gradients gq, gk, gv (and gdout when requested, else None)."""
     validate(q, k, v)
+    raise_pending(q.device)
     lib = load_library()
     q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
     zeros = None
@@ -355,6 +428,7 @@ def attn_bwd2_noalloc(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scal
     library's built-in array (b*h*t_pad <= NOALLOC_MAX_ROWS), for callers that may
     not allocate device memory while the op runs; only outputs are allocated here."""
     validate(q, k, v)
+    raise_pending(q.device)
     lib = load_library()
     q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
     uq, uk, uv = (prep(u.to(q.dtype)) for u in (uq, uk, uv))
@@ -421,6 +495,7 @@ def _from_p_args(p, ref, causal: bool, scale: float, **views) -> FromPArgs:
 def dv_from_p(p: torch.Tensor, dout: torch.Tensor) -> torch.Tensor:
     """dV = P^T dout for P [b, h, t, t] and dout [b, h, t, d] (every entry of P is read)."""
     _from_p_check(p, dout)
+    raise_pending(dout.device)
     lib = load_library()
     p, dout = prep_p(p.to(dout.dtype)), prep(dout)
     with torch.cuda.device(dout.device):
@@ -435,6 +510,7 @@ def dv_from_p(p: torch.Tensor, dout: torch.Tensor) -> torch.Tensor:
 def rowsum_from_p(p: torch.Tensor, dout: torch.Tensor, v: torch.Tensor, causal: bool) -> torch.Tensor:
     """rowsum[b, h, i] = sum_j P_ij (dout_i . v_j), fp32 [b, h, t]."""
     _from_p_check(p, dout, v)
+    raise_pending(dout.device)
     lib = load_library()
     p, dout, v = prep_p(p.to(dout.dtype)), prep(dout), prep(v)
     b, h, t, _ = dout.shape
@@ -450,6 +526,7 @@ def rowsum_from_p(p: torch.Tensor, dout: torch.Tensor, v: torch.Tensor, causal: 
 def dqdk_from_p(q, k, v, dout, p, rowsum, causal: bool, scale: float):
     """dq = scale dS k, dk = scale dS^T q with dS = P o (dout v^T - rowsum)."""
     _from_p_check(p, q, k, v, dout)
+    raise_pending(q.device)
     lib = load_library()
     q, k, v, dout = prep(q), prep(k), prep(v), prep(dout)
     p = prep_p(p.to(q.dtype))

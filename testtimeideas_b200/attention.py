@@ -12,9 +12,18 @@ gradients. Differences, all deliberate:
   reference's ``save_p*`` modes store P as a constant and drop the terms
   through P's dependence on q and k (backward_stubs.py:428-514); here the
   double backward is the closed form of d<dq,u_q>+<dk,u_k>+<dv,u_v>.
-* ``save_p`` / ``save_p_triton`` / ``save_p_triton_bwd`` / ``save_p_triton_full``
-  additionally materialize P in the forward (as the reference does) and keep
-  it on the context as ``ctx.saved_probs``.
+* The ``save_p`` / ``save_p_triton`` / ``save_p_triton_bwd`` /
+  ``save_p_triton_full`` modes run the same kernels as ``recompute`` and do
+  not materialize P. The reference saves the T x T probabilities in the
+  forward (triton_attention.py:270-273) and streams them in its backward
+  (:354-362) to avoid recomputing them; on B200 recomputing a score tile
+  from the saved row log-sum-exp costs a fraction of streaming it from HBM
+  (2*d flops against 2 bytes per entry: at d=64, 128 flops at ~1.3 PFLOP/s
+  against 2 bytes at ~6.5 TB/s, a quarter of the time), and the complete
+  second-order terms need the scores again anyway. The passes that do read
+  a materialized P remain available as the reference's from-P helpers
+  (``ttt_kernels.backward_stubs``), with the P-writing forward in
+  ``_lib.attn_fwd(..., save_p=True)``.
 * CPU tensors (and fp32 tensors on CPU) take the reference's math path:
   forward without a graph, backward recomputing ``_attention_math`` under
   autograd (triton_attention.py:416-420), so create_graph works there too.
@@ -88,22 +97,11 @@ class TritonAttentionFn(torch.autograd.Function):
         ctx.causal = bool(causal)
         ctx.scale = float(scale)
         ctx.bwd_mode = bwd_mode
-        ctx.saved_probs = ()
         ctx.on_gpu = _kernel_path(q)
         if not ctx.on_gpu:
             ctx.save_for_backward(q, k, v)
-            if bwd_mode in SAVE_P_MODES:
-                with torch.no_grad():
-                    scores = torch.matmul(q, k.transpose(-2, -1)) * scale
-                    if causal:
-                        t = scores.size(-1)
-                        mask = torch.triu(torch.ones((t, t), device=q.device, dtype=torch.bool), diagonal=1)
-                        scores = scores.masked_fill(mask, float("-inf"))
-                    ctx.saved_probs = (torch.softmax(scores, dim=-1),)
             return attention_math(q, k, v, causal, scale)
-        o, lse2, p = _lib.attn_fwd(q, k, v, ctx.causal, ctx.scale, save_p=bwd_mode in SAVE_P_MODES)
-        if p is not None:
-            ctx.saved_probs = (p,)
+        o, lse2, _ = _lib.attn_fwd(q, k, v, ctx.causal, ctx.scale)
         ctx.save_for_backward(q, k, v, o, lse2)
         return o
 

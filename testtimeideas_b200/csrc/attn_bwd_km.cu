@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   if (C::PAD == 0 && (smem_u32(smem_raw) & 1023u) != 0) {
     // no room to realign: refuse to run on a misaligned base (the swizzled
     // tiles would be read wrongly) and report it through the error word
-    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrMisaligned);
+    if (threadIdx.x == 0) report_error(p.err, p.err_host, kErrMisaligned);
     return;
   }
   uint8_t* sR = smem + C::OFF_R;
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const uint32_t tAcc0 = tmem + C::ACC_COL;  // dK / dd_K
   const uint32_t tAcc1 = tAcc0 + D;          // dV / dd_V
   const uint32_t tE = tmem + C::E_COL;       // packed E tiles (ETM)
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, p.err_host};
   // TMEM column of K-step kk (16 queries) of E tile j of tile n. Outside a
   // dedicated region each half of the elementwise warps (queries 32h..32h+31)
   // writes E only over score columns it has read itself: 32 columns of the first

@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   const uint32_t tQ = tmem + C::RES_COL;
   const uint32_t tDO = tQ + (C::RT_Q ? D / 2 : 0);
   const uint32_t tUQ = tDO + (C::RT_DO ? D / 2 : 0);
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, p.err_host};
 
   if (warp >= C::NCW) {
    if constexpr (C::SPLIT_REGS) regs_release<C::REG_CTRL>();

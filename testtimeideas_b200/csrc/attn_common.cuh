@@ -55,6 +55,7 @@ struct KParams {
   float scale;       // softmax scale applied to Q K^T
   float scale_log2;  // scale * log2(e)
   int* err;          // device error word (0 = ok), may be null
+  int* err_host;     // host-mapped mirror of the error word, may be null
   // Split mode (nsplit > 1; passes that support it): grid column x works on head
   // x / nsplit and on share x % nsplit of its block's tile stream, and writes
   // unscaled fp32 partial results part0 / part1, [nsplit][b*h][t_pad][d], in place

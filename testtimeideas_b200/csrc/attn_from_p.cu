@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(192, 1) attn_from_p_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, p.err_host};
 
   if (warp == 5) {
     // ------------------------------------------------------------ producer

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem;        // S buffers at columns 0 and 128
   const uint32_t tO = tmem + 256;  // O accumulator, D columns
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, p.err_host};
 
   if (warp == 5) {
     // ------------------------------------------------------------ producer
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd2_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, p.err_host};
 
   if (warp >= 8) {
    regs_release<C::REG_CTRL>();

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "ttt_attn.h"
+#include "host_ctx.h"
 #include "kernels.h"
 
 namespace {
@@ -136,6 +137,24 @@ int encode_p(CUtensorMap* m, const ttt_view& v, const ttt_problem& pb, int rows)
   return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
 }
 
+// Host-mapped mirrors of the device error word, one per context, registered by
+// ttt_attn_error_mirror. Kernels write a mirror only when they report an error.
+std::mutex g_mirror_mu;
+std::map<unsigned long long, int32_t*> g_mirror;
+bool g_any_mirror = false;  // read under g_mirror_mu; skips the context lookup while none is registered
+
+int32_t* error_mirror() {
+  {
+    std::lock_guard<std::mutex> lk(g_mirror_mu);
+    if (!g_any_mirror) return nullptr;
+  }
+  unsigned long long ctx = 0;
+  if (!ttt::current_context_id(&ctx)) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mirror_mu);
+  auto it = g_mirror.find(ctx);
+  return it == g_mirror.end() ? nullptr : it->second;
+}
+
 void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
   k.B = pb.b;
   k.H = pb.h;
@@ -146,6 +165,7 @@ void fill_common(KParams& k, const ttt_problem& pb, int32_t* err) {
   k.window_kind = pb.window_kind;
   k.scale_log2 = pb.scale * 1.4426950408889634f;
   k.err = err;
+  k.err_host = err != nullptr ? error_mirror() : nullptr;
 }
 
 void set_raw(KParams& k, int slot, const ttt_view& v) {
@@ -238,7 +258,9 @@ struct Side {
   cudaEvent_t fork = nullptr, join = nullptr;
 };
 std::mutex g_side_mu;
-std::map<int, Side> g_side;
+// One side stream per context (keyed by its id, so a device reset or a
+// non-primary context never receives a stream created in another context).
+std::map<unsigned long long, Side> g_side;
 
 // Overlap pays when a pass has too few CTAs to fill the GPU for long (under two
 // waves of one CTA per SM); with more, the passes' tails are short and running
@@ -353,10 +375,10 @@ class Fork {
       std::lock_guard<std::mutex> lk(g_prof_mu);
       if (g_prof_on) return;
     }
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    unsigned long long ctx = 0;
+    if (!ttt::current_context_id(&ctx)) return;
     std::lock_guard<std::mutex> lk(g_side_mu);
-    Side& sd = g_side[dev];
+    Side& sd = g_side[ctx];
     if (sd.stream == nullptr) {
       if (cudaStreamCreateWithFlags(&sd.stream, cudaStreamNonBlocking) != cudaSuccess) {
         sd.stream = nullptr;
@@ -414,6 +436,7 @@ const char* ttt_attn_status_string(int s) {
     case TTT_ERR_UNSUPPORTED: return "unsupported request";
     case TTT_ERR_SCRATCH: return "b*h*t_pad exceeds the fixed scratch of the allocation-free entry point";
     case TTT_ERR_SCRATCH_SETUP: return "could not obtain the device address of the built-in scratch array";
+    case TTT_ERR_MIRROR: return "the error mirror must be pinned host memory mapped at the same device address";
     default: return "unknown status";
   }
 }
@@ -750,6 +773,35 @@ int ttt_attn_profile_collect(int32_t* counts, double* total_ms, int n_kinds) {
     g_event_pool[r.device].push_back(r.stop);
   }
   return status;
+}
+
+int ttt_attn_error_mirror(int32_t* host_word) {
+  unsigned long long ctx = 0;
+  if (!ttt::current_context_id(&ctx)) return TTT_ERR_LAUNCH;
+  if (host_word != nullptr) {
+    if ((reinterpret_cast<uintptr_t>(host_word) & 3u) != 0) return TTT_ERR_ALIGN;
+    // kernels write it through the same address: pinned host memory mapped into
+    // the device's address space at that address (unified addressing)
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, host_word) != cudaSuccess || at.type != cudaMemoryTypeHost ||
+        at.devicePointer != static_cast<void*>(host_word))
+      return TTT_ERR_MIRROR;
+  }
+  std::lock_guard<std::mutex> lk(g_mirror_mu);
+  if (host_word != nullptr) {
+    g_mirror[ctx] = host_word;
+  } else {
+    g_mirror.erase(ctx);
+  }
+  g_any_mirror = !g_mirror.empty();
+  return TTT_OK;
+}
+
+int ttt_attn_selftest_wait(int64_t limit_ns, int32_t* err, void* stream) {
+  if (err == nullptr) return TTT_ERR_NULL;
+  if (limit_ns <= 0 || limit_ns > 10000000000LL) return TTT_ERR_SHAPE;
+  return launched(ttt::launch_selftest_wait(static_cast<unsigned long long>(limit_ns), err, error_mirror(),
+                                            static_cast<cudaStream_t>(stream)));
 }
 
 int ttt_attn_selftest_umma(const void* a, const void* b, float* c, int n, int k, int dtype, int mode, int32_t* err,

@@ -89,6 +89,10 @@ cudaError_t launch_fwd_combine(const FwdCombineArgs& a, cudaStream_t stream);
 // (MN-major, "accumulate" form); inputs through the same 4-D tensor maps.
 // With a_tmem the A tile is copied into TMEM and the product is issued with A
 // from TMEM (the TS form).
+// Runs one bounded mbarrier wait that nothing completes (limit_ns, then the
+// error word and its mirror receive kErrTimeout | (0xfe << 8)); see misc.cu.
+cudaError_t launch_selftest_wait(unsigned long long limit_ns, int* err, int* err_host, cudaStream_t stream);
+
 cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, const void* a, float* c, int n, int k,
                                  bool bf16, bool b_mn_major, bool a_tmem, int* err, cudaStream_t stream);
 

@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(128, 1) selftest_umma_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  Guard g{abort_flag, p.err};
+  Guard g{abort_flag, p.err, nullptr};
   if constexpr (A_TMEM) {
     // Row r of A (this thread's lane) into TMEM columns 256 .. 256+K/2, two
     // 16-bit elements per 32-bit column, low half first.
@@ -287,6 +287,33 @@ cudaError_t launch_selftest_umma(const CUtensorMap& ta, const CUtensorMap& tb, c
   if (!bf16 && b_mn_major) return launch(selftest_umma_kernel<false, true, false>);
   if (bf16 && !b_mn_major) return launch(selftest_umma_kernel<true, false, false>);
   return launch(selftest_umma_kernel<true, true, false>);
+}
+
+// Failure-path self-test of the bounded waits: one thread initializes an
+// mbarrier that expects one arrival and waits on its first phase with the same
+// mbar_wait every kernel uses, but with the caller's limit. Nothing arrives
+// and no TMA or UMMA work is in flight, so the wait runs out after limit_ns,
+// records kErrTimeout | (kSelftestWaitSite << 8) in the error word (and its
+// host-mapped mirror) and returns: the kernel ends normally, the context stays
+// usable.
+constexpr int kSelftestWaitSite = 0xfe;
+__global__ void __launch_bounds__(32, 1) selftest_wait_kernel(unsigned long long limit_ns, int* err, int* err_host) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  abort_flag = 0;
+  fence_mbar_init();
+  Guard g{&abort_flag, err, err_host};
+  if (mbar_wait(&bar, 0, g, kSelftestWaitSite, limit_ns)) {
+    // cannot happen (nothing arrives); reported so that a test would notice
+    report_error(err, err_host, kErrMisaligned);
+  }
+}
+
+cudaError_t launch_selftest_wait(unsigned long long limit_ns, int* err, int* err_host, cudaStream_t stream) {
+  selftest_wait_kernel<<<1, 32, 0, stream>>>(limit_ns, err, err_host);
+  return cudaGetLastError();
 }
 
 }  // namespace ttt

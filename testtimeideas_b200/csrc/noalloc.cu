@@ -23,12 +23,20 @@
 // In host code the array's name is a host-side stand-in, not a device address,
 // so it is never handed to a kernel directly: the first call on each device
 // (with that device current) obtains the device address with
-// cudaGetSymbolAddress, checks the result, and caches it. That first call
-// should come before any stream capture.
+// cudaGetSymbolAddress, checks the result, and caches it for the device's
+// context (a device reset or another context gets its own lookup). That first
+// call should come before any stream capture. Under lazy module loading (the
+// CUDA default since 12.2) it is also the moment the driver loads this file's
+// module and so allocates the array: a caller that may not allocate while it
+// runs makes one warm-up call per device during its set-up, or sets
+// CUDA_MODULE_LOADING=EAGER so that the array exists once the library's
+// module is loaded.
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 
+#include "host_ctx.h"
 #include "ttt_attn.h"
 
 namespace {
@@ -36,22 +44,22 @@ namespace {
 constexpr long long kMaxRows = TTT_ATTN_NOALLOC_MAX_ROWS;
 __device__ __align__(256) float g_bwd2_scratch[2 * kMaxRows];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-float* g_scratch[kMaxDevices] = {};
+std::map<unsigned long long, float*> g_scratch;  // context id -> device address of the array
 
-// Device address of the scratch array on the current device (set up once).
-int scratch_for_current_device(float** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TTT_ERR_SCRATCH_SETUP;
+// Device address of the scratch array in the current context (looked up once).
+int scratch_for_current_context(float** out) {
+  unsigned long long ctx = 0;
+  if (!ttt::current_context_id(&ctx)) return TTT_ERR_SCRATCH_SETUP;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (g_scratch[dev] == nullptr) {
+  auto it = g_scratch.find(ctx);
+  if (it == g_scratch.end()) {
     void* addr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&addr, g_bwd2_scratch);
     if (e != cudaSuccess || addr == nullptr) return TTT_ERR_SCRATCH_SETUP;
-    g_scratch[dev] = static_cast<float*>(addr);
+    it = g_scratch.emplace(ctx, static_cast<float*>(addr)).first;
   }
-  *out = g_scratch[dev];
+  *out = it->second;
   return TTT_OK;
 }
 
@@ -61,10 +69,14 @@ extern "C" int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream) {
   if (a == nullptr) return TTT_ERR_NULL;
   const ttt_problem& pb = a->pb;
   if (pb.b < 1 || pb.h < 1 || pb.t < 1 || pb.t > (1 << 22)) return TTT_ERR_SHAPE;
-  const long long rows = static_cast<long long>(pb.b) * pb.h * ttt_attn_t_pad(pb.t);
+  // b*h is bounded first (as every entry point bounds it), so the row count
+  // below cannot overflow: at most 2^31 * 2^22.
+  const long long bh = static_cast<long long>(pb.b) * pb.h;
+  if (bh > 0x7fffffffLL) return TTT_ERR_SHAPE;
+  const long long rows = bh * ttt_attn_t_pad(pb.t);
   if (rows > kMaxRows) return TTT_ERR_SCRATCH;
   float* scratch = nullptr;
-  const int s = scratch_for_current_device(&scratch);
+  const int s = scratch_for_current_context(&scratch);
   if (s != TTT_OK) return s;
   ttt_bwd2_args args = *a;
   args.gamma = scratch;

@@ -66,11 +66,24 @@ TTT_DEV uint32_t mbar_test(uint64_t* bar, uint32_t parity) {
 struct Guard {
   volatile int* abort;  // shared memory flag, set by the first wait that times out
   int* err;             // global error word (may be null)
+  int* err_host;        // host-mapped mirror of the error word (may be null)
 };
+
+// Record an error: the first code wins in the device word; the host-mapped
+// mirror (pinned host memory the binding registered) receives it too, so the
+// host sees it without synchronizing. Only error paths call this.
+TTT_DEV void report_error(int* err, int* err_host, int code) {
+  if (err) atomicCAS(err, 0, code);
+  if (err_host) {
+    *reinterpret_cast<volatile int*>(err_host) = code;
+    __threadfence_system();
+  }
+}
 
 // Bounded parity wait. Returns true when the phase with `parity` completed,
 // false if this CTA is aborting (timeout here or elsewhere in the CTA).
-TTT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const Guard& g, int site) {
+TTT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const Guard& g, int site,
+                       unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
@@ -82,9 +95,9 @@ TTT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const Guard& g, int site)
         *g.abort = 1;
         return false;
       }
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *g.abort = 1;
-        if (g.err) atomicCAS(g.err, 0, kErrTimeout | ((site & 0xff) << 8) | (blockIdx.x & 0xff));
+        report_error(g.err, g.err_host, kErrTimeout | ((site & 0xff) << 8) | (blockIdx.x & 0xff));
         return false;
       }
     }

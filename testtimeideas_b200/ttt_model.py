@@ -110,17 +110,15 @@ class TTTModel(nn.Module):
         return self.head(self.ln_f(x))
 
     def forward(self, input_ids=None, *, mode: str = "full", prefix_hidden=None):
-        if mode == "prefix":
-            if input_ids is None:
-                raise ValueError("input_ids required for prefix mode")
-            return self.prefix_forward(input_ids)
-        if mode == "suffix":
-            if prefix_hidden is None:
-                raise ValueError("prefix_hidden required for suffix mode")
-            return self.suffix_forward(prefix_hidden)
-        if input_ids is None:
-            raise ValueError("input_ids required for full mode")
-        return self.suffix_forward(self.prefix_forward(input_ids))
+        """Token ids to logits. mode="prefix" stops after the prefix blocks and returns
+        their hidden states; mode="suffix" starts from such states (prefix_hidden);
+        any other mode runs the whole model, as the reference's does."""
+        start_from_hidden = mode == "suffix"
+        given, what = (prefix_hidden, "prefix_hidden") if start_from_hidden else (input_ids, "input_ids")
+        if given is None:
+            raise ValueError(f"TTTModel.forward(mode={mode!r}) needs {what}")
+        hidden = prefix_hidden if start_from_hidden else self.prefix_forward(input_ids)
+        return hidden if mode == "prefix" else self.suffix_forward(hidden)
 
 
 def compute_loss(logits, targets, mask=None):
