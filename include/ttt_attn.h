@@ -20,10 +20,12 @@
  *    caller-owned device buffer of at least ttt_attn_work_bytes(pb) bytes,
  *    256-byte aligned, lets a pass whose grid is too small to fill the GPU
  *    (few heads, causal) split each CTA's stream of tiles over several CTAs
- *    and sum their fp32 partial results in a fixed order afterwards. With
- *    work == NULL or too small a buffer the pass runs unsplit. The two forms
- *    compute the same quantities; their fp32 summation orders differ, so the
- *    16-bit results may differ in the last bit.
+ *    and sum their fp32 partial results in a fixed order afterwards, and lets
+ *    the d = 64 first-order backward compute dQ inside its key-major pass.
+ *    With work == NULL or too small a buffer the passes run unsplit and dQ
+ *    gets its own pass. The forms compute the same quantities; their fp32
+ *    summation orders differ, so the 16-bit results may differ in the last
+ *    bit.
  *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
  *    stream); no entry point synchronizes the host.
  *  - Return value: TTT_OK or a ttt_status code. Argument errors are detected
@@ -229,6 +231,12 @@ int ttt_attn_bwd2_noalloc(const ttt_bwd2_args* a, void* stream);
  * host can poll it, e.g. at the entry of its next call. The library never
  * clears it; the caller does. */
 int ttt_attn_error_mirror(int32_t* host_word);
+/* The code in the mirror registered for the current context (0 when none is
+ * registered or no kernel has reported an error since the last take), which
+ * it clears. No synchronization: a report still in flight shows up at a later
+ * take. The caller also clears the device error word it passes to the passes
+ * (in stream order), or later launches that get it exit at once. */
+int ttt_attn_error_take(void);
 
 /* Test hook for the failure path (no reference counterpart): one kernel runs the
  * library's bounded mbarrier wait on a barrier that nothing completes, with a
@@ -241,12 +249,18 @@ int ttt_attn_selftest_wait(int64_t limit_ns, int32_t* err, void* stream);
 /* roundup(t, 128): the row count of every statistics array. */
 int ttt_attn_t_pad(int t);
 /* Bytes of work space with which every pass of problem *pb (forward,
- * backward, double backward with or without the dout gradient) can split its
- * work; 0 when none of them would split (enough CTAs to fill the GPU, or a
- * non-causal or banded problem, whose CTAs are of equal length). Depends on
- * the current device's SM count. No reference counterpart (the reference's
- * Triton launches pick their grid per call). */
+ * backward, double backward with or without the dout gradient) runs in its
+ * fastest form: the split slices of a causal problem over few heads (see
+ * ttt_attn_split_count), and, for d = 64, the fp32 dQ accumulator
+ * ([b*h][t_pad][d]) with which ttt_attn_bwd computes dQ inside its key-major
+ * pass instead of a second, query-major pass (whose dQ rows it adds in an
+ * unspecified order, so dq may differ from run to run in the last bit). 0 when
+ * neither applies. Depends on the current device's SM count. No reference
+ * counterpart (the reference's Triton launches pick their grid per call). */
 int64_t ttt_attn_work_bytes(const ttt_problem* pb);
+/* Number of shares each CTA's tile stream of the backward passes of *pb is
+ * split into when the work space is given (1: unsplit). */
+int ttt_attn_split_count(const ttt_problem* pb);
 /* Static description of a status code. */
 const char* ttt_attn_status_string(int status);
 /* TTT_ATTN_ABI_VERSION of the loaded library. */

@@ -52,15 +52,23 @@ def test_host_helpers(lib):
 
 
 def test_work_bytes_query(lib):
-    # invalid problems need no work space; without a GPU the SM count is unknown, so nothing splits
+    # invalid problems need no work space
     bad = _lib.Problem(1, 1, 128, 96, 0, 1, 0.125)
     assert lib.ttt_attn_work_bytes(ctypes.byref(bad)) == 0
     assert lib.ttt_attn_work_bytes(None) == 0
-    noncausal = _lib.Problem(1, 1, 16384, 64, 0, 0, 0.125)
-    assert lib.ttt_attn_work_bytes(ctypes.byref(noncausal)) == 0
+    assert lib.ttt_attn_split_count(None) == 1
+    # d = 128, non-causal: nothing splits and dQ keeps its own pass
+    wide = _lib.Problem(1, 1, 16384, 128, 0, 0, 0.125)
+    assert lib.ttt_attn_work_bytes(ctypes.byref(wide)) == 0
+    # d = 64: the fused backward's fp32 dQ accumulator [b*h][t_pad][d]
+    noncausal = _lib.Problem(2, 3, 1000, 64, 0, 0, 0.125)
+    assert lib.ttt_attn_split_count(ctypes.byref(noncausal)) == 1
+    assert lib.ttt_attn_work_bytes(ctypes.byref(noncausal)) == 2 * 3 * 1024 * 64 * 4
     if not torch.cuda.is_available():
+        # without a GPU the SM count is unknown, so nothing splits
         causal = _lib.Problem(1, 1, 16384, 64, 0, 1, 0.125)
-        assert lib.ttt_attn_work_bytes(ctypes.byref(causal)) == 0
+        assert lib.ttt_attn_split_count(ctypes.byref(causal)) == 1
+        assert lib.ttt_attn_work_bytes(ctypes.byref(causal)) == 16384 * 64 * 4
 
 
 def _fwd_args(**over):
@@ -258,3 +266,25 @@ def test_failure_hooks_validate_on_the_host(lib):
     assert lib.ttt_attn_selftest_wait(0, ctypes.addressof(word), None) == 4  # TTT_ERR_SHAPE: limit out of range
     assert lib.ttt_attn_selftest_wait(20_000_000_000, ctypes.addressof(word), None) == 4
     assert b"pinned host memory" in lib.ttt_attn_status_string(13)
+
+
+def test_torch_operators_register_with_shape_functions():
+    """libttt_torch.so loads without a GPU and registers ttt::fwd / bwd / bwd2, whose
+    shape functions let FakeTensor tracing (torch.compile) run without the kernels."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    if not _lib.TORCH_OPS_PATH.exists():
+        from testtimeideas_b200 import build
+        build.build_all()
+    _lib.load_torch_ops()
+    for name in ("fwd", "bwd", "bwd2", "error_word"):
+        assert hasattr(torch.ops.ttt, name), name
+    with FakeTensorMode():
+        q = torch.empty(2, 3, 200, 64, dtype=torch.bfloat16, device="cuda")
+        o, lse2 = torch.ops.ttt.fwd(q, q, q, True, 0.125)
+        assert o.shape == q.shape and o.dtype == q.dtype
+        assert lse2.shape == (6, 256) and lse2.dtype == torch.float32
+        dq, dk, dv, delta = torch.ops.ttt.bwd(q, q, q, o, q, lse2, True, 0.125)
+        assert dq.shape == dk.shape == dv.shape == q.shape and delta.shape == (6, 256)
+        gq, gk, gv, gdo = torch.ops.ttt.bwd2(q, q, q, q, lse2, delta, q, q, q, True, 0.125, True)
+        assert gq.shape == gk.shape == gv.shape == gdo.shape == q.shape
+        assert torch.ops.ttt.bwd2(q, q, q, q, lse2, delta, q, q, q, True, 0.125, False)[3].numel() == 0

@@ -13,7 +13,8 @@ Configurations (BASELINE.json):
             API in the reference sweep's mode (save_p_triton_full). The causal
             case runs every pass in split mode (each CTA's tile stream cut
             into shares, fp32 partials summed in order) and the forward's
-            combination kernel.
+            combination kernel; both run the first-order backward with dQ
+            inside the key-major pass (d = 64).
   config 4  T=16384 d=128 bf16 causal, 18 heads: the four-head launch groups
             of a full config-4 pass, including a partial group (18 = 4*4 + 2).
             Heads 0, 7 and 17 are compared with the oracle.
@@ -113,17 +114,17 @@ def _compare(case, dtype, got, ref, heads=None):
     assert not failures, f"{case}: " + "; ".join(failures)
 
 
-def _work_bytes(b, h, t, d, dtype, causal):
+def _split_count(b, h, t, d, dtype, causal):
     pb = _lib.Problem(b, h, t, d, _lib.TTT_BF16 if dtype == torch.bfloat16 else _lib.TTT_F16, 1 if causal else 0,
                       1.0 / math.sqrt(d))
-    return int(_lib.load_library().ttt_attn_work_bytes(ctypes.byref(pb)))
+    return int(_lib.load_library().ttt_attn_split_count(ctypes.byref(pb)))
 
 
 @pytest.mark.parametrize("causal", [True, False], ids=["causal", "noncausal"])
 def test_config3_t16384_public_api(causal):
     b, h, t, d, dtype = 1, 1, 16384, 64, torch.float16
     # the causal problem is the one that splits every pass over more CTAs
-    assert (_work_bytes(b, h, t, d, dtype, causal) > 0) == causal
+    assert (_split_count(b, h, t, d, dtype, causal) > 1) == causal
     x = _inputs(b, h, t, d, dtype, seed=303, scale_in=1.0)
     got = _public_step(x, causal, "save_p_triton_full")
     ref = _oracle_fp32(x, causal)
@@ -132,7 +133,7 @@ def test_config3_t16384_public_api(causal):
 
 def test_config4_sample_t16384_d128_bf16():
     b, h, t, d, dtype = 1, 18, 16384, 128, torch.bfloat16
-    assert _work_bytes(b, h, t, d, dtype, True) == 0  # enough CTAs: the unsplit grouped launch of config 4
+    assert _split_count(b, h, t, d, dtype, True) == 1  # enough CTAs: the unsplit grouped launch of config 4
     x = _inputs(b, h, t, d, dtype, seed=404, scale_in=0.5)
     got = _public_step(x, True, "recompute")
     heads = (0, 7, 17)

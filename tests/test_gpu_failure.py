@@ -50,9 +50,8 @@ def test_timeout_surfaces_at_the_next_op_and_library_recovers():
     _lib.check_device_errors(dev)
     x = _small_inputs()
     scale = 1.0 / math.sqrt(64)
-    _lib.attn_fwd(x["q"], x["k"], x["v"], True, scale)  # registers the host mirror for this device
+    _lib.attn_fwd(x["q"], x["k"], x["v"], True, scale)  # creates the error word and registers its host mirror
     torch.cuda.synchronize(dev)
-    assert dev.index in _lib._mirrors, "the host mirror of the error word was not registered"
     _lib.selftest_wait(LIMIT_NS, dev)
     torch.cuda.synchronize(dev)  # the failing kernel has finished; the next op issues no sync of its own
     with pytest.raises(_lib.KernelError, match="bounded wait"):

@@ -51,7 +51,8 @@ def test_meta_step_cuda_matches_cpu(window, suffix, chunk, pfilter):
     assert (num / den) ** 0.5 < 5e-2
     # the double backward runs when the inner gradient passes through attention (all
     # parameters updated); with only the last block's fast MLP updated it does not
-    kinds = ("fwd", "bwd_kv", "bwd_q") + (("bwd2_stats", "bwd2_q", "bwd2_kv") if pfilter is None else ())
+    # (head dim 64: dQ comes out of the key-major pass, so no separate query-major dQ pass runs)
+    kinds = ("fwd", "bwd_kv") + (("bwd2_stats", "bwd2_q", "bwd2_kv") if pfilter is None else ())
     for kind in kinds:
         assert prof[kind][0] > 0, kind
     if pfilter is not None:
@@ -95,6 +96,6 @@ def test_inference_adaptation_and_streaming_cuda_matches_cpu():
     assert len(stream) == len(ref_stream)
     for x, r in zip(stream, ref_stream):
         assert rel(x, r) < 3e-2
-    for kind in ("fwd", "bwd_kv", "bwd_q"):
+    for kind in ("fwd", "bwd_kv"):
         assert prof[kind][0] > 0, kind
     assert prof["bwd2_stats"][0] == 0

@@ -1,7 +1,13 @@
-"""ctypes binding of libttt_attn.so (include/ttt_attn.h) and the tensor-level ops.
+"""Bindings of libttt_attn.so (include/ttt_attn.h) and the tensor-level ops.
+
+The forward, backward and double backward run through the PyTorch operators
+ttt::fwd, ttt::bwd and ttt::bwd2 of libttt_torch.so (C++ over the C ABI; their
+shape functions are registered here, so torch.compile traces through them).
+The remaining entry points (P-materializing forward, passes over a given P,
+the allocation-free double backward, test hooks) are called through ctypes.
 
 Every op here runs the sm_100a kernels; there is no CPU or PyTorch fallback:
-if the library is missing or the tensors are not CUDA fp16/bf16 with
+if a library is missing or the tensors are not CUDA fp16/bf16 with
 d in {64, 128}, the op raises.
 """
 
@@ -17,6 +23,7 @@ import torch
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "_lib" / "libttt_attn.so"
+TORCH_OPS_PATH = _PKG / "_lib" / "libttt_torch.so"
 
 TTT_F16, TTT_BF16 = 0, 1
 _STATUS = {
@@ -68,7 +75,8 @@ class FromPArgs(ctypes.Structure):
 EXPORTED = ("ttt_attn_fwd", "ttt_attn_bwd", "ttt_attn_bwd2", "ttt_attn_t_pad", "ttt_attn_status_string",
             "ttt_attn_abi_version", "ttt_attn_selftest_umma", "ttt_attn_profile_enable", "ttt_attn_profile_collect",
             "ttt_attn_bwd2_noalloc", "ttt_attn_dv_from_p", "ttt_attn_rowsum_from_p", "ttt_attn_dqdk_from_p",
-            "ttt_attn_work_bytes", "ttt_attn_error_mirror", "ttt_attn_selftest_wait")
+            "ttt_attn_work_bytes", "ttt_attn_split_count", "ttt_attn_error_mirror", "ttt_attn_error_take",
+            "ttt_attn_selftest_wait")
 ERR_WORD_TIMEOUT = 0x40000000  # TTT_ERR_WORD_TIMEOUT
 SELFTEST_WAIT_SITE = 0xFE
 NOALLOC_MAX_ROWS = 1 << 20  # TTT_ATTN_NOALLOC_MAX_ROWS
@@ -100,12 +108,16 @@ def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         lib.ttt_attn_abi_version.restype = ctypes.c_int
         lib.ttt_attn_work_bytes.restype = ctypes.c_int64
         lib.ttt_attn_work_bytes.argtypes = [ctypes.c_void_p]
+        lib.ttt_attn_split_count.restype = ctypes.c_int
+        lib.ttt_attn_split_count.argtypes = [ctypes.c_void_p]
         lib.ttt_attn_selftest_umma.restype = ctypes.c_int
         lib.ttt_attn_selftest_umma.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_void_p]
         lib.ttt_attn_error_mirror.restype = ctypes.c_int
         lib.ttt_attn_error_mirror.argtypes = [ctypes.c_void_p]
+        lib.ttt_attn_error_take.restype = ctypes.c_int
+        lib.ttt_attn_error_take.argtypes = []
         lib.ttt_attn_selftest_wait.restype = ctypes.c_int
         lib.ttt_attn_selftest_wait.argtypes = [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         lib.ttt_attn_profile_enable.restype = ctypes.c_int
@@ -121,6 +133,65 @@ class KernelError(RuntimeError):
     pass
 
 
+_ops_loaded = False
+
+
+def load_torch_ops() -> None:
+    """Load libttt_torch.so (once): registers ttt::fwd, ttt::bwd, ttt::bwd2 and
+    ttt::error_word, and their shape functions. Raises if it has not been built."""
+    global _ops_loaded
+    if _ops_loaded:
+        return
+    with _lib_lock:
+        if _ops_loaded:
+            return
+        if not TORCH_OPS_PATH.exists():
+            raise RuntimeError(
+                f"{TORCH_OPS_PATH} not found: build the libraries first (python -m testtimeideas_b200.build)")
+        torch.ops.load_library(str(TORCH_OPS_PATH))
+        _register_fakes()
+        _ops_loaded = True
+
+
+def _register_fakes() -> None:
+    """Output shapes of the operators for tracing (FakeTensor / torch.compile)."""
+
+    @torch.library.register_fake("ttt::fwd")
+    def _fwd(q, k, v, causal, scale, window=0, window_kind=0, split=True):
+        b, h, t, d = q.shape
+        return q.new_empty((b, h, t, d)), q.new_empty((b * h, t_pad(t)), dtype=torch.float32)
+
+    @torch.library.register_fake("ttt::bwd")
+    def _bwd(q, k, v, o, dout, lse2, causal, scale, window=0, window_kind=0, split=True):
+        b, h, t, d = q.shape
+        return (q.new_empty((b, h, t, d)), q.new_empty((b, h, t, d)), q.new_empty((b, h, t, d)),
+                q.new_empty((b * h, t_pad(t)), dtype=torch.float32))
+
+    @torch.library.register_fake("ttt::bwd2")
+    def _bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal, scale, need_gdout, window=0, window_kind=0,
+              split=True):
+        b, h, t, d = q.shape
+        return (q.new_empty((b, h, t, d)), q.new_empty((b, h, t, d)), q.new_empty((b, h, t, d)),
+                q.new_empty((b, h, t, d)) if need_gdout else q.new_empty((0,)))
+
+    @torch.library.register_fake("ttt::error_word")
+    def _err(device):
+        return torch.empty((1,), dtype=torch.int32, device=device)
+
+
+def _op(fn, *args):
+    """Call an operator; a failure it reports from the library becomes KernelError."""
+    if torch.compiler.is_compiling():
+        return fn(*args)
+    try:
+        return fn(*args)
+    except RuntimeError as e:
+        msg = str(e)
+        if "libttt_attn" in msg:
+            raise KernelError(msg.splitlines()[0]) from None
+        raise
+
+
 def _check(status: int) -> None:
     if status != 0:
         msg = load_library().ttt_attn_status_string(status).decode()
@@ -132,14 +203,14 @@ def t_pad(t: int) -> int:
 
 
 # ---------------------------------------------------------------- device error word
-# Per device: the int32 error word the kernels report into (device memory), and
-# a pinned host mirror of it that the library registers for the device's
-# context (ttt_attn_error_mirror). A kernel that gives up on a bounded wait
-# writes the mirror too, so every op checks it at entry without synchronizing:
-# a timeout surfaces as KernelError at the first op the host issues after the
-# failing kernel reported it (check_device_errors synchronizes and checks).
+# Per device, libttt_torch.so owns the int32 error word the kernels report into
+# (device memory) and a pinned host mirror of it, registered with the library
+# for the device's context (ttt_attn_error_mirror). A kernel that gives up on a
+# bounded wait writes the mirror too, so every op checks it at entry without
+# synchronizing: a timeout surfaces as KernelError at the first op the host
+# issues after the failing kernel reported it (check_device_errors also
+# synchronizes and reads the word itself).
 _err_words: dict[int, torch.Tensor] = {}
-_mirrors: dict[int, tuple[torch.Tensor, ctypes.c_int32]] = {}
 
 
 def _dev_index(device: torch.device | None) -> int:
@@ -152,28 +223,10 @@ def error_word(device: torch.device) -> torch.Tensor:
     idx = _dev_index(device)
     w = _err_words.get(idx)
     if w is None:
-        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        load_torch_ops()
+        w = torch.ops.ttt.error_word(torch.device("cuda", idx))
         _err_words[idx] = w
-        _register_mirror(idx)
     return w
-
-
-def _register_mirror(idx: int) -> None:
-    host = torch.zeros(1, dtype=torch.int32).pin_memory()
-    with _on(torch.device("cuda", idx)):
-        status = load_library().ttt_attn_error_mirror(host.data_ptr())
-    if status != 0:  # the mirror is an addition: without it, errors still surface at check_device_errors
-        return
-    _mirrors[idx] = (host, ctypes.c_int32.from_address(host.data_ptr()))
-
-
-def _clear(idx: int) -> None:
-    m = _mirrors.get(idx)
-    if m is not None:
-        m[1].value = 0
-    w = _err_words.get(idx)
-    if w is not None:
-        w.zero_()
 
 
 def raise_pending(device: torch.device | None = None) -> None:
@@ -181,30 +234,31 @@ def raise_pending(device: torch.device | None = None) -> None:
     to the host mirror; no synchronization. Clears both words (the device word in
     stream order), so that later launches run again."""
     idx = _dev_index(device)
-    m = _mirrors.get(idx)
-    if m is None or m[1].value == 0:
-        return
-    code = m[1].value
+    if idx not in _err_words:
+        return  # no op has run on this device yet
     with _on(torch.device("cuda", idx)):
-        _clear(idx)
+        code = load_library().ttt_attn_error_take()
+        if code == 0:
+            return
+        _err_words[idx].zero_()
     raise KernelError(f"libttt_attn kernel gave up on a bounded wait on cuda:{idx} (error word 0x{code:08x}); "
                       "results of the calls since then are invalid")
 
 
 def check_device_errors(device: torch.device | None = None) -> None:
     """Synchronize and raise if any kernel on `device` gave up on a bounded wait."""
-    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    idx = _dev_index(dev)
+    dev = torch.device("cuda", _dev_index(device))
     w = error_word(dev)
     torch.cuda.synchronize(dev)
-    code = int(w.item())
-    m = _mirrors.get(idx)
-    if code == 0 and m is not None:
-        code = m[1].value
-    if code != 0:
-        with _on(torch.device("cuda", idx)):
-            _clear(idx)
+    with _on(dev):
+        code = int(w.item())
+        pending = load_library().ttt_attn_error_take()
+        if code == 0:
+            code = pending
+        if code != 0:
+            w.zero_()
             torch.cuda.synchronize(dev)
+    if code != 0:
         raise KernelError(f"libttt_attn kernel timeout on {dev} (error word 0x{code:08x})")
 
 
@@ -254,12 +308,18 @@ def view(x: torch.Tensor | None) -> View:
 WINDOW_KINDS = {"sliding": 0, "chunk": 1}
 
 
-def problem(q: torch.Tensor, causal: bool, scale: float, window=0) -> Problem:
+def window_args(window=0) -> tuple[int, int]:
     """window: 0, an int W (sliding: key j visible to query i iff i - W < j <= i) or
-    a (W, kind) pair with kind "sliding" or "chunk" (chunk-local, see include/ttt_attn.h)."""
-    b, h, t, d = q.shape
+    a (W, kind) pair with kind "sliding" or "chunk" (chunk-local, see include/ttt_attn.h);
+    returns (W, kind code)."""
     w, kind = (window, "sliding") if isinstance(window, int) else window
-    return Problem(b, h, t, d, _dtype_code(q), 1 if causal else 0, float(scale), int(w), WINDOW_KINDS[kind])
+    return int(w), WINDOW_KINDS[kind]
+
+
+def problem(q: torch.Tensor, causal: bool, scale: float, window=0) -> Problem:
+    b, h, t, d = q.shape
+    w, kind = window_args(window)
+    return Problem(b, h, t, d, _dtype_code(q), 1 if causal else 0, float(scale), w, kind)
 
 
 def validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -316,8 +376,22 @@ def default_scale(d: int) -> float:
 
 
 # ---------------------------------------------------------------- ops
-def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: int = 0):
-    """O, lse2 (fp32 [b*h, t_pad]) and, with save_p, P ([b, h, t, t])."""
+def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: int = 0, split: bool = True):
+    """O, lse2 (fp32 [b*h, t_pad]) and, with save_p, P ([b, h, t, t]; else None).
+    split=False keeps small causal problems unsplit (see include/ttt_attn.h)."""
+    if save_p:
+        return _attn_fwd_with_p(q, k, v, causal, scale, window)
+    validate(q, k, v)
+    load_torch_ops()
+    w, kind = window_args(window)
+    o, lse2 = _op(torch.ops.ttt.fwd, q, k, v, bool(causal), float(scale), w, kind, bool(split))
+    if _SYNC_CHECK:
+        check_device_errors(q.device)
+    return o, lse2, None
+
+
+def _attn_fwd_with_p(q, k, v, causal: bool, scale: float, window: int = 0):
+    """The forward that also writes P (for the from-P helpers), through the C ABI."""
     validate(q, k, v)
     raise_pending(q.device)
     lib = load_library()
@@ -327,71 +401,45 @@ def attn_fwd(q, k, v, causal: bool, scale: float, save_p: bool = False, window: 
         o = torch.empty((b, h, t, d), dtype=q.dtype, device=q.device)
         lse2 = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
         # causal: the kernel writes only key tiles up to the diagonal; the rest stays zero
-        p = (torch.zeros if causal else torch.empty)((b, h, t, t), dtype=q.dtype, device=q.device) if save_p else None
+        p = (torch.zeros if causal else torch.empty)((b, h, t, t), dtype=q.dtype, device=q.device)
         pb = problem(q, causal, scale, window)
         work, wptr, wbytes = work_space(pb, q.device)
-        args = FwdArgs(pb, view(q), view(k), view(v), view(o), lse2.data_ptr(),
-                       p.data_ptr() if p is not None else None, error_word(q.device).data_ptr(), wptr, wbytes)
+        args = FwdArgs(pb, view(q), view(k), view(v), view(o), lse2.data_ptr(), p.data_ptr(),
+                       error_word(q.device).data_ptr(), wptr, wbytes)
         _check(lib.ttt_attn_fwd(ctypes.byref(args), _stream()))
         if _SYNC_CHECK:
             check_device_errors(q.device)
     return o, lse2, p
 
 
-def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0):
+def attn_bwd(q, k, v, o, dout, lse2, causal: bool, scale: float, window: int = 0, split: bool = True):
     """dq, dk, dv and delta = rowsum(dout o o) (fp32 [b*h, t_pad])."""
     validate(q, k, v)
-    raise_pending(q.device)
-    lib = load_library()
-    q, k, v, o, dout = prep(q), prep(k), prep(v), prep(o), prep(dout.to(q.dtype))
-    b, h, t, d = q.shape
-    with _on(q.device):
-        dq, dk, dv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
-        delta = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
-        pb = problem(q, causal, scale, window)
-        work, wptr, wbytes = work_space(pb, q.device)
-        args = BwdArgs(pb, view(q), view(k), view(v), view(o), view(dout),
-                       lse2.data_ptr(), delta.data_ptr(), view(dq), view(dk), view(dv),
-                       error_word(q.device).data_ptr(), wptr, wbytes)
-        _check(lib.ttt_attn_bwd(ctypes.byref(args), _stream()))
-        if _SYNC_CHECK:
-            check_device_errors(q.device)
+    load_torch_ops()
+    w, kind = window_args(window)
+    dq, dk, dv, delta = _op(torch.ops.ttt.bwd, q, k, v, o, dout, lse2, bool(causal), float(scale), w, kind,
+                            bool(split))
+    if _SYNC_CHECK:
+        check_device_errors(q.device)
     return dq, dk, dv, delta
 
 
 def attn_bwd2(q, k, v, dout, lse2, delta, uq, uk, uv, causal: bool, scale: float, need_gdout: bool,
-              window: int = 0):
-    """Second-order gradients gq, gk, gv (and gdout when requested, else None)."""
+              window: int = 0, split: bool = True):
+    """Second-order gradients gq, gk, gv (and gdout when requested, else None).
+    A probe given as None is zero."""
     validate(q, k, v)
-    raise_pending(q.device)
-    lib = load_library()
-    q, k, v, dout = prep(q), prep(k), prep(v), prep(dout.to(q.dtype))
+    load_torch_ops()
     zeros = None
-
-    def probe(u):
-        nonlocal zeros
-        if u is None:
-            if zeros is None:
-                zeros = torch.zeros_like(q, memory_format=torch.contiguous_format)
-            return zeros
-        return prep(u.to(q.dtype))
-
-    uq, uk, uv = probe(uq), probe(uk), probe(uv)
-    b, h, t, d = q.shape
-    with _on(q.device):
-        gq, gk, gv = (torch.empty_like(q, memory_format=torch.contiguous_format) for _ in range(3))
-        gdout = torch.empty_like(q, memory_format=torch.contiguous_format) if need_gdout else None
-        gamma = torch.empty((b * h, t_pad(t)), dtype=torch.float32, device=q.device)
-        rho = torch.empty_like(gamma)
-        pb = problem(q, causal, scale, window)
-        work, wptr, wbytes = work_space(pb, q.device)
-        args = Bwd2Args(pb, view(q), view(k), view(v), view(dout), lse2.data_ptr(),
-                        delta.data_ptr(), view(uq), view(uk), view(uv), gamma.data_ptr(), rho.data_ptr(),
-                        view(gq), view(gk), view(gv), view(gdout), error_word(q.device).data_ptr(), wptr, wbytes)
-        _check(lib.ttt_attn_bwd2(ctypes.byref(args), _stream()))
-        if _SYNC_CHECK:
-            check_device_errors(q.device)
-    return gq, gk, gv, gdout
+    if uq is None or uk is None or uv is None:
+        zeros = torch.zeros_like(q, memory_format=torch.contiguous_format)
+    uq, uk, uv = (zeros if u is None else u for u in (uq, uk, uv))
+    w, kind = window_args(window)
+    gq, gk, gv, gdout = _op(torch.ops.ttt.bwd2, q, k, v, dout, lse2, delta, uq, uk, uv, bool(causal), float(scale),
+                            bool(need_gdout), w, kind, bool(split))
+    if _SYNC_CHECK:
+        check_device_errors(q.device)
+    return gq, gk, gv, (gdout if need_gdout else None)
 
 
 def selftest_umma(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool, a_tmem: bool = False) -> torch.Tensor:

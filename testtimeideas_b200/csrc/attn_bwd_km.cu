@@ -7,6 +7,13 @@
 //             (replaces _attn_bwd_dv_from_p_kernel and _attn_bwd_dk_kernel,
 //             ttt_kernels/backward_stubs.py:124-151 and 313-359, recomputing P
 //             from lse2 instead of reading it)
+//   kBwdKVQ : kBwdKV plus dQ = scale * dS K in the same pass (d = 64): the
+//             elementwise warps also write dS^T to shared memory; every pair
+//             of 64-query tiles gets one dS K product (M = 128 queries, both
+//             operands MN-major), whose rows the elementwise warps add into an
+//             fp32 dQ accumulator in global memory two tiles later. It replaces
+//             the separate query-major dQ pass (kBwdQ), which recomputes S, P,
+//             dP and dS for the same tiles.
 //   kBwd2KV : dd_K = scale * (dS^T u_q + G_S^T Q),  dd_V = G_dP^T dO
 //             (the key-side half of the complete double backward that the
 //             reference approximates with torch.matmul in
@@ -59,6 +66,13 @@ struct KmCfg {
   static constexpr int BK = 128;  // keys per CTA (TMEM lanes)
   static constexpr int BM = 64;   // queries per streamed tile
   static constexpr bool BWD2 = (KIND == kBwd2KV);
+  static constexpr bool FUSEQ = (KIND == kBwdKVQ);
+  static_assert(!FUSEQ || D == 64, "the fused dQ pass is built for d = 64 (its TMEM fits beside two score buffers)");
+  // FUSEQ: a dQ accumulator of D columns for the 128 queries of a pair of tiles,
+  // and the pair's dS^T tiles in shared memory (two pair buffers).
+  static constexpr int DQ_COLS = FUSEQ ? D : 0;
+  static constexpr int TILE_DS = BK * BM * 2;
+  static constexpr int DS_BYTES = FUSEQ ? 4 * TILE_DS : 0;
   static constexpr int NR = BWD2 ? 4 : 2;   // resident: K, V, (u_k, u_v)
   static constexpr int NSC = BWD2 ? 4 : 2;  // score tiles: S^T, (G_dS^T,) dP^T, ((dO u_v^T)^T)
   static constexpr int NE = BWD2 ? 3 : 2;   // P^T, dS^T | dS^T, G_S^T, G_dP^T
@@ -87,7 +101,7 @@ struct KmCfg {
   // TMEM layout
   static constexpr bool E_OWN = !BWD2;  // E over the S^T columns of its own score buffer
   static constexpr bool ETM = BWD2;     // E in a region of its own (dedicated or shared)
-  static constexpr int NBUF_WANT = (2 * NSC * BM + NA * D + (ETM ? NE * E_COLS : 0) <= 512) ? 2 : 1;
+  static constexpr int NBUF_WANT = (2 * NSC * BM + NA * D + DQ_COLS + (ETM ? NE * E_COLS : 0) <= 512) ? 2 : 1;
   static constexpr int NBUF = NBUF_WANT;
   static constexpr int SC_COLS = NBUF * NSC * BM;
   static constexpr int ACC_COL = SC_COLS;
@@ -123,15 +137,20 @@ struct KmCfg {
       NCT + (SPLIT_REGS ? 128 : 64) + (TWO_ISSUERS && !SPLIT_REGS ? 32 : 0) + (THREE_ISSUERS ? 64 : 0);
   static constexpr int E_COL = E_DEDICATED ? SC_COLS + NA * D : (E_OVERLAP ? 2 * BM : 0);
   static_assert(!E_OVERLAP || BWD2, "E over score columns only in the double backward");
-  static constexpr int TMEM_USED = SC_COLS + NA * D + (E_DEDICATED ? NE * E_COLS : 0);
+  static constexpr int DQ_COL = SC_COLS + NA * D;  // FUSEQ: the pair's dQ accumulator
+  static constexpr int TMEM_USED = SC_COLS + NA * D + DQ_COLS + (E_DEDICATED ? NE * E_COLS : 0);
+  static_assert(!FUSEQ || (NBUF == 2 && !E_DEDICATED), "fused dQ layout");
   static constexpr int TMEM_COLS = TMEM_USED <= 128 ? 128 : (TMEM_USED <= 256 ? 256 : 512);
   static_assert(TMEM_USED <= 512, "TMEM overflow");
   static_assert(!E_OVERLAP || NBUF == 1, "overlapping E needs a single score buffer");
-  static constexpr int BAR_BYTES = 22 * 8;
-  static constexpr int FIXED = NR * TILE_R + BAR_BYTES + (STAGE_TX - STAGE);
+  // barriers 0..20; FUSEQ adds dq_full and dq_empty; then the TMEM slot and abort flag
+  static constexpr int NBAR = FUSEQ ? 25 : 21;
+  static constexpr int BAR_BYTES = (NBAR + 1) * 8;
+  static constexpr int FIXED = NR * TILE_R + DS_BYTES + BAR_BYTES + (STAGE_TX - STAGE);
   static constexpr int NSTAGE = (FIXED + 4 * STAGE + 1024 <= 232448) ? 4 : (FIXED + 3 * STAGE + 1024 <= 232448) ? 3 : 2;
   static constexpr int OFF_R = 0;
-  static constexpr int OFF_S = OFF_R + NR * TILE_R;
+  static constexpr int OFF_DS = OFF_R + NR * TILE_R;
+  static constexpr int OFF_S = OFF_DS + DS_BYTES;
   static constexpr int OFF_BAR = OFF_S + (NSTAGE - 1) * STAGE + STAGE_TX;  // the last stage needs no padding
   static constexpr int BODY = OFF_BAR + BAR_BYTES;
   // Reserve room to realign the dynamic shared-memory base to 1024 bytes when
@@ -186,8 +205,23 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   // e_cons[b]: the accumulate products that read E in score buffer b completed
   // (two issuers, E over its own score buffer)
   uint64_t* e_cons = bars + 19;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  // FUSEQ: dq_full (the dS K product of a pair completed: its TMEM rows are ready
+  // and its dS^T tiles may be reused) and dq_empty (NCT arrivals: the compute
+  // warps have read those rows, so the next pair's product may overwrite them)
+  uint64_t* dq_full = bars + 21;
+  uint64_t* dq_empty = bars + 22;
+  // FUSEQ: stage_full (NCT arrivals: every row of a pair's dQ is staged for the TMA
+  // reduce) and stage_free (one arrival: the TMA unit finished reading a staged
+  // buffer, which the next pair's dS^T may then overwrite). Bounded waits, so a CTA
+  // that aborts never leaves a warp parked at a hardware barrier.
+  uint64_t* stage_full = bars + 23;
+  uint64_t* stage_free = bars + 24;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* sDS = smem + C::OFF_DS;
+  // dS^T of tile n ([BK keys x BM queries], PL layout): pair buffer (n / 2) % 2, half n % 2,
+  // so a pair's two tiles form one [BK x 2 BM] MN-major operand
+  auto dsT = [&](int n) { return sDS + (((n >> 1) & 1) * 2 + (n & 1)) * C::TILE_DS; };
   auto tileR = [&](int t) { return sR + t * C::TILE_R; };
   auto st0 = [&](int s) { return sS + s * C::STAGE; };
   auto st1 = [&](int s) { return sS + s * C::STAGE + C::ST0_BYTES; };
@@ -215,6 +249,12 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 21; ++i) mbar_init(bars + i, 1);
+    if (C::FUSEQ) {
+      mbar_init(dq_full, 1);
+      mbar_init(dq_empty, C::NCT);
+      mbar_init(stage_full, C::NCT);
+      mbar_init(stage_free, 1);
+    }
     mbar_init(s_free + 0, C::NCT);
     mbar_init(s_free + 1, C::NCT);
     if (C::SPLIT_SCORES) {  // both issuers' score products
@@ -249,6 +289,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   const uint32_t tAcc0 = tmem + C::ACC_COL;  // dK / dd_K
   const uint32_t tAcc1 = tAcc0 + D;          // dV / dd_V
   const uint32_t tE = tmem + C::E_COL;       // packed E tiles (ETM)
+  const uint32_t tDQ = tmem + C::DQ_COL;     // FUSEQ: dQ rows of the current pair
   Guard g{abort_flag, p.err, p.err_host};
   // TMEM column of K-step kk (16 queries) of E tile j of tile n. Outside a
   // dedicated region each half of the elementwise warps (queries 32h..32h+31)
@@ -407,6 +448,22 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
               if (me == 1) umma_commit(e_cons + (n - 1) % NBUF);
             }
             umma_commit(l_empty + (n - 1) % NSTAGE);
+            if constexpr (C::FUSEQ) {
+              // after the last tile of a pair: dQ rows of its 128 queries = dS K, with
+              // A = the pair's dS^T tiles read MN-major (rows = keys) and B = K (MN-major);
+              // the rows of a missing second tile are never read back
+              if (me == 1 && (((n - 1) & 1) || n == n_tiles)) {
+                const int pr = (n - 1) >> 1;
+                if (pr >= 1 && !(ok = mbar_wait(dq_empty, (pr - 1) & 1, g, 11))) break;
+                tc_fence_after();
+                constexpr uint32_t id_dq = idesc_f16(128, D, BF16, true, true);
+                const uint32_t aDS = smem_u32(dsT(2 * pr));
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                  umma_ss(tDQ, desc_mnmajor(aDS, BK, kk), desc_mnmajor(aK, BK, kk), id_dq, kk > 0 ? 1u : 0u);
+                umma_commit(dq_full);
+              }
+            }
           }
         }
         if ((me == 1 || C::ACC_SPLIT) && ok) umma_commit(acc_full);
@@ -482,11 +539,62 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
     // query tiles ending past the last query that sees the block's first key need the band mask
     const int band_last = CAUSAL ? band.last_query(k0) : 0x3fffffff;
     const F2 C2 = f2s(c), SC2 = f2s(scale);
+    // FUSEQ: add the dQ rows of pair pr into the fp32 accumulator. TMEM lane r holds
+    // query 2*pr*BM + r of this share's tiles; each thread stages its half of the
+    // row (fp32) into the pair's dS^T buffer, which the pair's product has finished
+    // reading, as two 128-byte-swizzled [128 x 32] panels (conflict-free 16-byte
+    // stores), and one thread has the TMA unit add both panels into the accumulator
+    // (a reduce in L2, asynchronous to these warps). Rows of a second tile the
+    // share does not have are staged as zeros; rows past t_pad are clipped by the map.
+    [[maybe_unused]] auto dq_drain = [&](int pr) -> bool {
+      if (!mbar_wait(dq_full, pr & 1, g, 12)) return false;
+      tc_fence_after();
+      float v[D / 2];
+      tmem_ld_nw<D / 2>(tDQ + lane_off + half * (D / 2), v);
+      tmem_wait_ld();
+      reg_fence(v);
+      tc_fence_before();
+      mbar_arrive(dq_empty);  // the rows are in registers: the next pair's product may overwrite them
+      const bool have = 2 * pr + (r >= BM ? 1 : 0) < n_tiles;
+      uint8_t* row = dsT(2 * pr) + half * (BK * 128) + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 x = have ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3])
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(row + ((c ^ (r & 7)) << 4)) = x;
+      }
+      fence_async_smem();
+      mbar_arrive(stage_full);
+      if (threadIdx.x == 0) {
+        // every row of both panels is staged
+        if (!mbar_wait(stage_full, pr & 1, g, 13)) return false;
+        const int q0 = (qt0 + 2 * pr) * BM;
+        tma_reduce_add_3d(&p.st[2], dsT(2 * pr), 0, q0, bh);
+        tma_reduce_add_3d(&p.st[2], dsT(2 * pr) + BK * 128, 32, q0, bh);
+        bulk_commit();
+      }
+      return true;
+    };
+    // Before tile n (even, n >= 4) writes dS^T into the pair buffer that pair
+    // n/2 - 2 staged its dQ rows in, the TMA unit must have finished reading them
+    // (thread 0 issued that reduce; it is its only bulk group still reading).
+    [[maybe_unused]] auto ds_reuse = [&](int n) -> bool {
+      if (threadIdx.x == 0) {
+        bulk_wait_read();
+        mbar_arrive(stage_free);
+      }
+      return mbar_wait(stage_free, ((n >> 1) - 2) & 1, g, 14);
+    };
     bool ok = true;
     for (int n = 0; n < n_tiles; ++n) {
       const int sb = n % NBUF, s = n % NSTAGE;
       const int qt = qt0 + n;
       const int qcol0 = qt * BM + c0;
+      if constexpr (C::FUSEQ) {
+        // pair (n - 3) / 2, whose product was issued about two tiles ago; draining it
+        // here also frees its dS^T buffer before the next pair's tiles are written
+        if ((n & 1) && n >= 3 && !dq_drain((n - 3) >> 1)) { ok = false; break; }
+      }
       if constexpr (C::THREE_ISSUERS) {
         // Two phases: S^T and G_dS^T come from issuer 0 well before dP^T and
         // (dO u_v^T)^T, which follow the previous tile's accumulate products;
@@ -658,6 +766,12 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
       // accumulate products have read it. E over score columns needs no wait: the
       // products that overwrite those columns are issued after this tile's e_full.
       if (C::E_DEDICATED && n >= 1 && !mbar_wait(e_empty, (n - 1) & 1, g, 7)) { ok = false; break; }
+      if constexpr (C::FUSEQ) {
+        // dS^T (unscaled, 16-bit) for the pair's dS K product; the async proxy reads it
+        if (!(n & 1) && n >= 4 && !ds_reuse(n)) { ok = false; break; }
+        store_cols<BF16, CPW>(dsT(n), BK, r, c0, dp);
+        fence_async_smem();
+      }
       {
         // this thread's 16 words of E tile j (see e_col)
         auto e_put = [&](int j) -> uint32_t {
@@ -682,6 +796,20 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         tc_fence_before();
       }
       mbar_arrive(e_full + (n & 1));
+    }
+    if constexpr (C::FUSEQ) {
+      // the pairs not drained in the loop (the last one or two); before acc_full, which
+      // issuer 1 commits only after its last dS K product
+      if (ok) {
+        const int drained = n_tiles >= 3 ? (n_tiles - 2) >> 1 : 0;
+        for (int pr = drained; pr < ((n_tiles + 1) >> 1); ++pr)
+          if (!dq_drain(pr)) {
+            ok = false;
+            break;
+          }
+      }
+      // the accumulator additions complete (and stop reading shared memory) before the CTA ends
+      if (threadIdx.x == 0) bulk_wait_all();
     }
     if (ok && mbar_wait(acc_full, 0, g, 8)) {
       tc_fence_after();
@@ -730,6 +858,9 @@ cudaError_t launch_km(const KParams& p, int d, bool bf16, bool causal, int kind,
 #define TTT_KM_KIND(D_, BF_, CA_)                                                  \
   if (d == D_ && bf16 == BF_ && causal == CA_) {                                   \
     if (kind == kBwdKV) return launch_km_t<D_, BF_, CA_, kBwdKV>(p, stream);       \
+    if constexpr (D_ == 64) {                                                      \
+      if (kind == kBwdKVQ) return launch_km_t<D_, BF_, CA_, kBwdKVQ>(p, stream);   \
+    }                                                                              \
     if (kind == kBwd2KV) return launch_km_t<D_, BF_, CA_, kBwd2KV>(p, stream);     \
   }
 #define TTT_KM_CA(D_, BF_) TTT_KM_KIND(D_, BF_, false) TTT_KM_KIND(D_, BF_, true)

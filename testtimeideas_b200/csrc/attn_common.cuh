@@ -23,6 +23,7 @@ enum Kind : int {
   kBwd2Q = 2,    // dd_q (+ dd_dO) of the double backward (query-major)
   kBwdKV = 3,    // dK, dV (key-major)
   kBwd2KV = 4,   // dd_k, dd_v of the double backward (key-major)
+  kBwdKVQ = 5,   // dK, dV and dQ in one key-major pass (dQ added into an fp32 accumulator)
 };
 
 struct KParams {
@@ -63,6 +64,10 @@ struct KParams {
   int nsplit;
   float* part0;
   float* part1;
+  // kBwdKVQ: fp32 dQ accumulator [b*h][t_pad][d], zero before the pass; every
+  // key block adds its dS K rows into it (unscaled), through the tensor map
+  // st[2] (dims d, t_pad, b*h; box 32 x 128 x 1, 128-byte swizzle).
+  float* acc_q;
 };
 
 // Launch order of a pass's CTAs, a grid of (units, blocks) with units = heads

@@ -143,6 +143,13 @@ TTT_DEV uint32_t issue_ts(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, 
   }
 }
 
+// Fire-and-forget vector add of four floats into global memory (the
+// reduction happens in L2); dst must be 16-byte aligned.
+TTT_DEV void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 // Named barrier 1 over the compute warps only (the producer and MMA warps
 // never take part).
 template <int NTHREADS>

@@ -103,6 +103,21 @@ int encode_stats(CUtensorMap* m, const float* p, int bh, int t_pad, int cols) {
   return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
 }
 
+// 3-D map over the fp32 dQ accumulator [bh][t_pad][d] of the fused backward:
+// dims (d, t_pad, bh), box (32, 128, 1), 128-byte swizzle; the kernel adds
+// [128 x 32] boxes into it (TMA reduce), rows past t_pad clipped.
+int encode_acc_q(CUtensorMap* m, float* acc, int bh, int t_pad, int d) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TTT_ERR_DRIVER;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(t_pad), static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 4, static_cast<cuuint64_t>(t_pad) * d * 4};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, acc, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TTT_OK : TTT_ERR_TENSOR_MAP;
+}
+
 // P view [b, h, t, t]: row stride p.st >= t, head strides; all multiples of 8.
 int check_p_view(const ttt_view& v, const ttt_problem& pb) {
   if (v.ptr == nullptr) return TTT_ERR_NULL;
@@ -315,9 +330,18 @@ int64_t fwd_work_need(const ttt_problem& pb) {
   const int n = split_count(pb, 256);
   return n > 1 ? static_cast<int64_t>(n) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * (pb.d + 2) * 4 : 0;
 }
-int64_t work_need(const ttt_problem& pb) {
+// Split slices of the backward passes, in bytes (0 when no pass splits).
+int64_t bwd_split_bytes(const ttt_problem& pb) {
   const int n = split_count(pb);
-  const int64_t bwd = n > 1 ? kWorkSlices * slice_floats(pb, n) * 4 : 0;
+  return n > 1 ? kWorkSlices * slice_floats(pb, n) * 4 : 0;
+}
+// The fp32 dQ accumulator [b*h][t_pad][d] of the fused first-order backward
+// (d = 64: dQ inside the key-major pass), placed after the split slices.
+int64_t acc_q_bytes(const ttt_problem& pb) {
+  return pb.d == 64 ? static_cast<int64_t>(pb.b) * pb.h * ttt_attn_t_pad(pb.t) * pb.d * 4 : 0;
+}
+int64_t work_need(const ttt_problem& pb) {
+  const int64_t bwd = bwd_split_bytes(pb) + acc_q_bytes(pb);
   const int64_t fwd = fwd_work_need(pb);
   return bwd > fwd ? bwd : fwd;
 }
@@ -326,16 +350,24 @@ struct Work {
   int nsplit = 1;  // 1: run unsplit
   float* base = nullptr;
   int64_t slice = 0;
+  float* acc_q = nullptr;  // the fused first-order backward's dQ accumulator (null: two passes)
   float* at(int i) const { return base + i * slice; }
 };
+// Each use of the work space needs its own part to fit: a buffer sized for the
+// split slices alone still splits the passes.
 Work plan_work(const ttt_problem& pb, void* work, int64_t work_bytes) {
   Work w;
+  if (work == nullptr || (reinterpret_cast<uintptr_t>(work) & 255u) != 0) return w;
   const int n = split_count(pb);
-  if (n <= 1 || work == nullptr || work_bytes < work_need(pb) || (reinterpret_cast<uintptr_t>(work) & 255u) != 0)
-    return w;
-  w.nsplit = n;
-  w.base = static_cast<float*>(work);
-  w.slice = slice_floats(pb, n);
+  const int64_t split_b = bwd_split_bytes(pb);
+  if (n > 1 && work_bytes >= split_b) {
+    w.nsplit = n;
+    w.base = static_cast<float*>(work);
+    w.slice = slice_floats(pb, n);
+  }
+  const int64_t acc_b = acc_q_bytes(pb);
+  if (acc_b > 0 && work_bytes >= split_b + acc_b)
+    w.acc_q = reinterpret_cast<float*>(static_cast<char*>(work) + split_b);
   return w;
 }
 void use_work(KParams& k, const Work& w, int first_slice) {
@@ -419,6 +451,11 @@ int ttt_attn_abi_version(void) { return TTT_ATTN_ABI_VERSION; }
 int64_t ttt_attn_work_bytes(const ttt_problem* pb) {
   if (pb == nullptr || check_problem(*pb) != TTT_OK) return 0;
   return work_need(*pb);
+}
+
+int ttt_attn_split_count(const ttt_problem* pb) {
+  if (pb == nullptr || check_problem(*pb) != TTT_OK) return 1;
+  return split_count(*pb);
 }
 
 const char* ttt_attn_status_string(int s) {
@@ -520,6 +557,35 @@ int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {
   }
 
   const Work w = plan_work(pb, a->work, a->work_bytes);
+  if (w.acc_q != nullptr) {
+    // One key-major pass for dK, dV and dQ: dQ rows are added into the zeroed fp32
+    // accumulator, then scaled and converted (the split reduction with one share).
+    const size_t acc_bytes = static_cast<size_t>(acc_q_bytes(pb));
+    if (cudaMemsetAsync(w.acc_q, 0, acc_bytes, s) != cudaSuccess) return TTT_ERR_LAUNCH;
+    KParams k;
+    std::memset(&k, 0, sizeof(k));
+    fill_common(k, pb, a->err);
+    TTT_TRY(encode_view(&k.own[0], a->k, pb, 128));
+    TTT_TRY(encode_view(&k.own[1], a->v, pb, 128));
+    const int rows = ttt::km_tile_rows(pb.d, ttt::kBwdKVQ);
+    TTT_TRY(encode_view(&k.str[0], a->q, pb, rows));
+    TTT_TRY(encode_view(&k.str[1], a->dout, pb, rows));
+    TTT_TRY(encode_stats(&k.st[0], a->lse2, bh, t_pad, rows));
+    TTT_TRY(encode_stats(&k.st[1], a->delta, bh, t_pad, rows));
+    set_out0(k, a->dk);
+    set_out1(k, a->dv);
+    use_work(k, w, 0);
+    k.acc_q = w.acc_q;
+    TTT_TRY(encode_acc_q(&k.st[2], w.acc_q, bh, t_pad, pb.d));
+    ProfScope prof(TTT_K_BWD_KV, s);
+    TTT_TRY(launched(ttt::launch_km(k, pb.d, bf16, causal, ttt::kBwdKVQ, s)));
+    if (w.nsplit > 1) TTT_TRY(reduce_splits(w, 0, pb, 2, a->dk, pb.scale, &a->dv, 1.f, s));
+    Work acc;
+    acc.nsplit = 1;
+    acc.base = w.acc_q;
+    acc.slice = 0;
+    return reduce_splits(acc, 0, pb, 1, a->dq, pb.scale, nullptr, 0.f, s);
+  }
   Fork fork(s, overlap_pays(pb));
   // dK, dV: key-major.
   {
@@ -795,6 +861,22 @@ int ttt_attn_error_mirror(int32_t* host_word) {
   }
   g_any_mirror = !g_mirror.empty();
   return TTT_OK;
+}
+
+int ttt_attn_error_take(void) {
+  unsigned long long ctx = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mirror_mu);
+    if (!g_any_mirror) return 0;
+  }
+  if (!ttt::current_context_id(&ctx)) return 0;
+  std::lock_guard<std::mutex> lk(g_mirror_mu);
+  auto it = g_mirror.find(ctx);
+  if (it == g_mirror.end()) return 0;
+  volatile int32_t* w = it->second;
+  const int32_t code = *w;
+  if (code != 0) *w = 0;
+  return code;
 }
 
 int ttt_attn_selftest_wait(int64_t limit_ns, int32_t* err, void* stream) {

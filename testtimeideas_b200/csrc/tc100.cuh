@@ -127,6 +127,22 @@ TTT_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c
       : "memory");
 }
 
+// 3-D tiled reduce-add of a shared-memory box into global memory (fp32 add in
+// L2 by the TMA unit), tracked by this thread's bulk async-group. The
+// coordinates are never negative here.
+TTT_DEV void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+      : "memory");
+}
+TTT_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's bulk groups have finished reading shared memory /
+// have completed entirely.
+TTT_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+TTT_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor core / TMA) before signalling the consumer.
 TTT_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
