@@ -782,7 +782,7 @@ int ttt_attn_dqdk_from_p(const ttt_from_p_args* a, void* stream) {
   const bool bf16 = pb.dtype == TTT_BF16, causal = pb.causal != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   {
-    // dK: key-major, V resident, P / dO / Q streamed per 64 queries
+    // dK: key-major, V resident, P / dO / Q streamed per 128 queries
     KParams k;
     std::memset(&k, 0, sizeof(k));
     fill_common(k, pb, a->err);
@@ -796,7 +796,7 @@ int ttt_attn_dqdk_from_p(const ttt_from_p_args* a, void* stream) {
     TTT_TRY(launched(ttt::launch_from_p(k, pb.d, bf16, causal, ttt::kFpDK, s)));
   }
   {
-    // dQ: query-major, dO resident, P / V / K streamed per 64 keys
+    // dQ: query-major, dO resident, P / V / K streamed per 128 keys
     KParams k;
     std::memset(&k, 0, sizeof(k));
     fill_common(k, pb, a->err);

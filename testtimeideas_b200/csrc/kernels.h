@@ -25,10 +25,12 @@ enum FpMode : int {
   kFpDK = 2,      // dK = scale dS^T Q              (own[0] = V, str[1] = dO, str[2] = Q, delta = rowsum [b*h, t])
   kFpDQ = 3,      // dQ = scale dS K                (own[0] = dO, str[1] = V, str[2] = K, delta = rowsum [b*h, t])
 };
-// Rows of the P box each mode expects (the streamed tiles of kFpDK use 64 rows,
-// the others 128).
-inline int from_p_box_rows(int mode) { return mode == kFpDK ? 64 : 128; }
-inline int from_p_stream_rows(int mode) { return (mode == kFpDK || mode == kFpDQ) ? 64 : 128; }
+// Streamed rows per step of each from-P pass (measured best: 128 for the
+// product-only passes and for kFpDK, 64 for kFpDQ).
+constexpr int from_p_step_rows(int mode) { return mode == kFpDQ ? 64 : 128; }
+// Rows of the P box and of the streamed [rows x d] tiles each mode expects.
+inline int from_p_box_rows(int mode) { return mode == kFpDK ? from_p_step_rows(mode) : 128; }
+inline int from_p_stream_rows(int mode) { return from_p_step_rows(mode); }
 cudaError_t launch_from_p(const KParams& p, int d, bool bf16, bool causal, int mode, cudaStream_t stream);
 
 // delta[bh, t] = sum_d dO[b,h,t,d] * O[b,h,t,d] for t < T, 0 for T <= t < t_pad.

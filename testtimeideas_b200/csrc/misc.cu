@@ -10,35 +10,71 @@
 
 namespace ttt {
 
-// One warp per row; lanes read D/32 consecutive elements each.
+// D/8 threads per row, each reading 16 bytes of O and of dO (rows start
+// 16-byte aligned: the views' base pointers are 16-byte aligned and their
+// strides are multiples of 8 elements). A warp covers 32/(D/8) rows per
+// iteration and issues the loads of UNROLL iterations before using any, so
+// each SM keeps enough bytes in flight to stream at HBM rate; the grid is a
+// few CTAs per SM striding over all rows.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) attn_delta_kernel(DeltaArgs a) {
+  constexpr int TPR = D / 8;            // threads per row
+  constexpr int RPW = 32 / TPR;         // rows per warp per iteration
+  constexpr int UNROLL = 4;
+  constexpr int RPB = 8 * RPW * UNROLL; // rows per CTA per pass
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  const int sub = lane / TPR, c8 = (lane % TPR) * 8;
   const int64_t total = static_cast<int64_t>(a.B) * a.H * a.t_pad;
-  if (row >= total) return;
-  const int bh = static_cast<int>(row / a.t_pad);
-  const int t = static_cast<int>(row % a.t_pad);
-  float acc = 0.f;
-  if (t < a.T) {
-    const int b = bh / a.H, h = bh % a.H;
-    const uint16_t* o = a.o + b * a.o_sb + h * a.o_sh + static_cast<int64_t>(t) * a.o_st;
-    const uint16_t* d = a.dout + b * a.d_sb + h * a.d_sh + static_cast<int64_t>(t) * a.d_st;
-    constexpr int PER = D / 32;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * RPB; base < total;
+       base += static_cast<int64_t>(gridDim.x) * RPB) {
+    uint4 ov[UNROLL], dv[UNROLL];
+    int64_t rows[UNROLL];
+    bool live[UNROLL];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int col = lane * PER + i;
-      acc += to_f32<BF16>(o[col]) * to_f32<BF16>(d[col]);
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t row = base + (static_cast<int64_t>(u) * 8 + warp) * RPW + sub;
+      rows[u] = row;
+      const int bh = static_cast<int>(row / a.t_pad);
+      const int t = static_cast<int>(row % a.t_pad);
+      live[u] = row < total && t < a.T;
+      ov[u] = make_uint4(0u, 0u, 0u, 0u);
+      dv[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (live[u]) {
+        const int b = bh / a.H, h = bh % a.H;
+        ov[u] = __ldg(reinterpret_cast<const uint4*>(a.o + b * a.o_sb + h * a.o_sh + static_cast<int64_t>(t) * a.o_st + c8));
+        dv[u] = __ldg(reinterpret_cast<const uint4*>(a.dout + b * a.d_sb + h * a.d_sh + static_cast<int64_t>(t) * a.d_st + c8));
+      }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    for (int u = 0; u < UNROLL; ++u) {
+      const uint32_t* ow = reinterpret_cast<const uint32_t*>(&ov[u]);
+      const uint32_t* dw = reinterpret_cast<const uint32_t*>(&dv[u]);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc = fmaf(to_f32<BF16>(static_cast<uint16_t>(ow[i] & 0xffffu)), to_f32<BF16>(static_cast<uint16_t>(dw[i] & 0xffffu)), acc);
+        acc = fmaf(to_f32<BF16>(static_cast<uint16_t>(ow[i] >> 16)), to_f32<BF16>(static_cast<uint16_t>(dw[i] >> 16)), acc);
+      }
+#pragma unroll
+      for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane % TPR == 0 && rows[u] < total) a.delta[rows[u]] = live[u] ? acc : 0.f;
+    }
   }
-  if (lane == 0) a.delta[row] = acc;
 }
 
 cudaError_t launch_delta(const DeltaArgs& a, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(a.B) * a.H * a.t_pad;
-  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  // SM count per device ordinal, looked up once (a stale entry only resizes the grid)
+  static int sm_of[64] = {0};
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) sms = sm_of[dev];
+  if (sms <= 0) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    if (dev >= 0 && dev < 64) sm_of[dev] = sms;
+  }
+  const int rpb = 8 * (32 / (a.D / 8)) * 4;
+  const int64_t need = (rows + rpb - 1) / rpb;
+  const dim3 grid(static_cast<unsigned>(need < 8LL * sms ? need : 8LL * sms));
   if (a.D == 64 && !a.bf16) attn_delta_kernel<64, false><<<grid, 256, 0, stream>>>(a);
   else if (a.D == 64 && a.bf16) attn_delta_kernel<64, true><<<grid, 256, 0, stream>>>(a);
   else if (a.D == 128 && !a.bf16) attn_delta_kernel<128, false><<<grid, 256, 0, stream>>>(a);

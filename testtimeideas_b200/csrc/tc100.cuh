@@ -118,6 +118,15 @@ TTT_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c
       : "memory");
 }
 
+// Bring a 4-D tile into L2 ahead of its load (no shared memory, no barrier):
+// a later tma_load_4d of the same box then reads it from L2.
+TTT_DEV void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // 2-D tiled load (coordinates innermost first).
 TTT_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
