@@ -320,7 +320,6 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
       const float own_rs = (MODE == kFpDQ && row < T) ? rs[row] : 0.f;
       for (int n = 0; n < n_tiles; ++n) {
         const int s = n % NSTAGE, sb = n & 1, eb = n & 1;
-        const int c0 = (n_first + n) * W + half * CW;  // first streamed index of this warp's columns
         if (!mbar_wait(s_full + sb, (n >> 1) & 1, g, 6)) { ok = false; break; }
         tc_fence_after();
         float dp[CW];
