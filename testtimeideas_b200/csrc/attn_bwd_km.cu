@@ -485,6 +485,10 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             umma_commit(l_empty + s);
             continue;
           }
+          // The stage of tile n (read next by this issuer's score product) is probed in the
+          // same batch as tile n-1's accumulate products, so a stage that already landed
+          // costs no separate wait on this thread (it sits on the tile-to-tile chain).
+          bool stage_seen = false;
           if (n >= 1) {
             // the accumulate products of tile n-1 read its E, written over this issuer's score columns
             if (!(ok = mbar_wait(e_full + ((n - 1) & 1), ((n - 1) >> 1) & 1, g, 4))) break;
@@ -492,23 +496,25 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             const int sp = (n - 1) % NSTAGE;
             const uint32_t bQ = smem_u32(st0(sp)), bDO = smem_u32(st1(sp)), bUQ = bQ + BM * 128;
             const uint32_t acc_first = n > 1 ? 1u : 0u;
-#pragma unroll
-            for (int kk = 0; kk < BM / 16; ++kk) {
-              const uint32_t a = (acc_first || kk > 0) ? 1u : 0u;
-              if (me == 1) {
-                // dd_K += dS^T u_q + G_S^T Q
-                umma_ts(tAcc0, e_col(0, kk, n - 1), desc_mnmajor(bUQ, SR0, kk), id_acc, a);
-                umma_ts(tAcc0, e_col(1, kk, n - 1), desc_mnmajor(bQ, SR0, kk), id_acc, 1u);
-              } else {
-                // dd_V += G_dP^T dO
-                umma_ts(tAcc1, e_col(2, kk, n - 1), desc_mnmajor(bDO, BM, kk), id_acc, a);
-              }
+            const uint64_t* pbar = n < n_tiles ? l_full + s : done;
+            const uint32_t ppar = n < n_tiles ? static_cast<uint32_t>((n / NSTAGE) & 1) : 0u;
+            static_assert(BM / 16 == 4, "the batched accumulate issue covers four K-steps");
+            uint32_t seen;
+            if (me == 1) {
+              // dd_K += dS^T u_q + G_S^T Q (K-steps of the two products interleaved)
+              seen = umma_ts_pair4_probe<LE>(tAcc0, e_col(0, 0, n - 1), desc_mnmajor(bUQ, SR0, 0), e_col(1, 0, n - 1),
+                                             desc_mnmajor(bQ, SR0, 0), id_acc, acc_first, pbar, ppar, done, 0u);
+            } else {
+              // dd_V += G_dP^T dO
+              seen = umma_ts4_probe<LE>(tAcc1, e_col(2, 0, n - 1), desc_mnmajor(bDO, BM, 0), id_acc, acc_first, pbar,
+                                        ppar, done, 0u);
             }
+            stage_seen = (seen & 1u) != 0;
             umma_commit(l_empty + sp);
           }
           if (n < n_tiles) {
             // dP^T = V dO^T (issuer 1) or (dO u_v^T)^T = u_v dO^T (issuer 2) over the E just read
-            if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (!stage_seen && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
             tc_fence_after();
             const uint32_t b1 = smem_u32(st1(s)), a0 = me == 1 ? aV : aUV;
             const uint32_t dcol = tmem + (me == 1 ? C::C_DP : C::C_UV);

@@ -451,6 +451,38 @@ TTT_DEV uint32_t umma_ts8_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t i
   return r0 | (r1 << 1);
 }
 
+// Two products into one accumulator, A from TMEM, their four K-steps
+// interleaved (A0 B0, A1 B1 for each K-step), issued as one batch behind two
+// barrier probes. Unlike umma_ss8_probe the probes use the non-suspending
+// mbarrier.test_wait, so an incomplete phase never delays the UMMAs. Only the
+// very first UMMA takes acc_first; every later one accumulates.
+template <class L>
+TTT_DEV uint32_t umma_ts_pair4_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t a1, uint64_t b1, uint32_t idesc,
+                                      uint32_t acc_first, const uint64_t* bar0, uint32_t par0, const uint64_t* bar1,
+                                      uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %11, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %12, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], [%9], %10, %12, t;\n\t"
+      "add.u32 ta, %7, %13; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "add.u32 ta, %9, %13; add.s64 db, %10, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "add.u32 ta, %7, %14; add.s64 db, %8, %17; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "add.u32 ta, %9, %14; add.s64 db, %10, %17; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "add.u32 ta, %7, %15; add.s64 db, %8, %18; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "add.u32 ta, %9, %15; add.s64 db, %10, %18; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %12, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(a1), "l"(b1),
+        "r"(acc_first), "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::b(1)), "n"(L::b(2)),
+        "n"(L::b(3))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
 // Byte offset of element (r, c) in PL(R, C) (16-bit elements).
 TTT_DEV uint32_t pl_offset(int R, int r, int c) {
   const int panel = c >> 6;
