@@ -506,8 +506,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
                                              desc_mnmajor(bQ, SR0, 0), id_acc, acc_first, pbar, ppar, done, 0u);
             } else {
               // dd_V += G_dP^T dO
-              seen = umma_ts4_probe<LE>(tAcc1, e_col(2, 0, n - 1), desc_mnmajor(bDO, BM, 0), id_acc, acc_first, pbar,
-                                        ppar, done, 0u);
+              seen = umma_ts4_tprobe<LE>(tAcc1, e_col(2, 0, n - 1), desc_mnmajor(bDO, BM, 0), id_acc, acc_first, pbar,
+                                         ppar, done, 0u);
             }
             stage_seen = (seen & 1u) != 0;
             umma_commit(l_empty + sp);

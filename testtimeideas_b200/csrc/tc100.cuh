@@ -451,6 +451,30 @@ TTT_DEV uint32_t umma_ts8_probe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t i
   return r0 | (r1 << 1);
 }
 
+// umma_ts4_probe with non-suspending probes (mbarrier.test_wait): for a barrier
+// that may still be incomplete when the batch is issued, where a suspending
+// try_wait would hold back the UMMAs behind it.
+template <class L>
+TTT_DEV uint32_t umma_ts4_tprobe(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t acc_first,
+                                 const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1) {
+  uint32_t r0, r1;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, q, t;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p0, [%2], %3;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p1, [%4], %5;\n\t"
+      "setp.ne.b32 q, %9, 0;\n\tsetp.eq.b32 t, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%6], [%7], %8, %10, q;\n\t"
+      "add.u32 ta, %7, %11; add.s64 db, %8, %14; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %12; add.s64 db, %8, %15; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "add.u32 ta, %7, %13; add.s64 db, %8, %16; tcgen05.mma.cta_group::1.kind::f16 [%6], [ta], db, %10, t;\n\t"
+      "selp.u32 %0, 1, 0, p0;\n\tselp.u32 %1, 1, 0, p1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(smem_u32(bar0)), "r"(par0), "r"(smem_u32(bar1)), "r"(par1), "r"(d), "r"(a0), "l"(b0), "r"(acc_first),
+        "r"(idesc), "n"(L::a(1)), "n"(L::a(2)), "n"(L::a(3)), "n"(L::b(1)), "n"(L::b(2)), "n"(L::b(3))
+      : "memory");
+  return r0 | (r1 << 1);
+}
+
 // Two products into one accumulator, A from TMEM, their four K-steps
 // interleaved (A0 B0, A1 B1 for each K-step), issued as one batch behind two
 // barrier probes. Unlike umma_ss8_probe the probes use the non-suspending
