@@ -92,7 +92,9 @@ typedef struct {
 /* Forward. Writes o and lse2 (base-2 log-sum-exp of scale*log2(e)*q k^T per
  * row; rows t..t_pad-1 get +inf). If p != NULL also writes the normalized
  * probabilities P as [b*h, t, t] 16-bit row-major (entries of causal key tiles
- * past the diagonal tile are left unwritten).
+ * past the diagonal tile are left unwritten): for t % 8 == 0 by a second pass
+ * after the row-LSE forward (which then may run split, as without P), for
+ * other t by a single forward kernel.
  * Replaces: ttt_kernels/triton_attention.py:278-337 (_attn_fwd_kernel,
  * _attn_fwd_kernel_stats, _attn_probs_kernel launches) and the probability
  * forward of the save_p modes, triton_attention.py:51-59 and 270-273. */

@@ -28,7 +28,8 @@ LIB = LIBDIR / "libttt_attn.so"
 TORCH_SRC = CSRC / "torch_ops.cpp"
 TORCH_LIB = LIBDIR / "libttt_torch.so"
 
-SOURCES = ["capi.cu", "attn_fwd.cu", "attn_bwd_qm.cu", "attn_bwd_km.cu", "misc.cu", "noalloc.cu", "attn_from_p.cu"]
+SOURCES = ["capi.cu", "attn_fwd.cu", "attn_bwd_qm.cu", "attn_bwd_km.cu", "misc.cu", "noalloc.cu", "attn_from_p.cu",
+           "attn_pwrite.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]

@@ -8,7 +8,9 @@
 //
 // Two kernels: attn_fwd2_kernel (below, two query tiles per CTA, P kept in
 // tensor memory) computes O and lse2; attn_fwd_kernel (this one) is used only
-// when the normalized P is also materialized (save_p modes).
+// when the normalized P is also materialized and T % 8 != 0 (for other T the
+// row-LSE forward is followed by attn_pwrite_kernel, attn_pwrite.cu, which
+// stores P by TMA).
 //
 // attn_fwd_kernel: one CTA owns 128 query rows of one head and streams 128-key tiles:
 //   warp 5      TMA producer: Q once, then K/V tiles into a 2-stage ring.

@@ -499,8 +499,12 @@ int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
   k.out_f0 = a->lse2;
   k.out1 = static_cast<uint16_t*>(a->p);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // split mode (the forward without P only): shares of each CTA's key stream
-  const int nf = a->p == nullptr ? split_count(pb, 256) : 1;
+  // P with T % 8 == 0: the row-LSE forward (split like the forward without P),
+  // then a pass that recomputes S and stores P by TMA; other T keep the
+  // single-kernel forward that writes P itself
+  const bool pwrite = a->p != nullptr && (pb.t % 8) == 0;
+  // split mode (the forward without a P epilogue only): shares of each CTA's key stream
+  const int nf = (a->p == nullptr || pwrite) ? split_count(pb, 256) : 1;
   const bool split = nf > 1 && a->work != nullptr && a->work_bytes >= fwd_work_need(pb) &&
                      (reinterpret_cast<uintptr_t>(a->work) & 255u) == 0;
   const int64_t o_floats = static_cast<int64_t>(nf) * pb.b * pb.h * ttt_attn_t_pad(pb.t) * pb.d;
@@ -510,17 +514,29 @@ int ttt_attn_fwd(const ttt_fwd_args* a, void* stream) {
     k.part1 = k.part0 + o_floats;
   }
   ProfScope prof(TTT_K_FWD, s);
-  TTT_TRY(launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr, s)));
-  if (!split) return TTT_OK;
-  ttt::FwdCombineArgs c;
-  c.part_o = k.part0;
-  c.part_ml = reinterpret_cast<const float2*>(k.part1);
-  c.out = static_cast<uint16_t*>(a->o.ptr);
-  c.sb = a->o.sb, c.sh = a->o.sh, c.st = a->o.st;
-  c.lse2 = a->lse2;
-  c.nsplit = nf, c.B = pb.b, c.H = pb.h, c.T = pb.t, c.t_pad = ttt_attn_t_pad(pb.t), c.D = pb.d;
-  c.bf16 = pb.dtype == TTT_BF16;
-  return launched(ttt::launch_fwd_combine(c, s));
+  TTT_TRY(launched(ttt::launch_fwd(k, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, a->p != nullptr && !pwrite, s)));
+  if (split) {
+    ttt::FwdCombineArgs c;
+    c.part_o = k.part0;
+    c.part_ml = reinterpret_cast<const float2*>(k.part1);
+    c.out = static_cast<uint16_t*>(a->o.ptr);
+    c.sb = a->o.sb, c.sh = a->o.sh, c.st = a->o.st;
+    c.lse2 = a->lse2;
+    c.nsplit = nf, c.B = pb.b, c.H = pb.h, c.T = pb.t, c.t_pad = ttt_attn_t_pad(pb.t), c.D = pb.d;
+    c.bf16 = pb.dtype == TTT_BF16;
+    TTT_TRY(launched(ttt::launch_fwd_combine(c, s)));
+  }
+  if (!pwrite) return TTT_OK;
+  KParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  fill_common(kp, pb, a->err);
+  TTT_TRY(encode_view(&kp.own[0], a->q, pb, 128));
+  TTT_TRY(encode_view(&kp.str[0], a->k, pb, 128));
+  // P is contiguous [b, h, t, t]
+  const ttt_view pv{a->p, static_cast<int64_t>(pb.h) * pb.t * pb.t, static_cast<int64_t>(pb.t) * pb.t, pb.t};
+  TTT_TRY(encode_p(&kp.str[1], pv, pb, 128));
+  kp.lse2 = a->lse2;
+  return launched(ttt::launch_pwrite(kp, pb.d, pb.dtype == TTT_BF16, pb.causal != 0, s));
 }
 
 int ttt_attn_bwd(const ttt_bwd_args* a, void* stream) {

@@ -8,6 +8,10 @@
 namespace ttt {
 
 cudaError_t launch_fwd(const KParams& p, int d, bool bf16, bool causal, bool save_p, cudaStream_t stream);
+// The normalized P of the save_p forward after the row-LSE forward: own[0] = Q,
+// str[0] = K, str[1] = P (map of encode_p, box 64 x 128), lse2 = the forward's
+// rows; requires T % 8 == 0.
+cudaError_t launch_pwrite(const KParams& p, int d, bool bf16, bool causal, cudaStream_t stream);
 // Query-major passes: kind in {kBwdQ, kStats, kBwd2Q}; gdo selects dd_dO output (kBwd2Q only).
 cudaError_t launch_qm(const KParams& p, int d, bool bf16, bool causal, int kind, bool gdo, cudaStream_t stream);
 // Key-major passes: kind in {kBwdKV, kBwd2KV}.
