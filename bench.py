@@ -377,12 +377,14 @@ def soak(step, x: dict, causal: bool, seconds: float, flush: Optional[torch.Tens
     same clock state."""
     t0 = time.perf_counter()
     n = 0
+    held = None  # the previous step's outputs, alive while the next step runs (as in the timed loop)
     while time.perf_counter() - t0 < seconds:
         if flush is not None:
             flush.fill_(1)
-        step(x, causal)
+        held = step(x, causal)
         torch.cuda.synchronize()
         n += 1
+    del held
     return {"steps": n, "seconds": round(time.perf_counter() - t0, 2)}
 
 
@@ -770,10 +772,15 @@ def run_ours(args, cfg: dict) -> None:
     # The clock sampler starts (and settles) before the warm-up steps, which then
     # bring the GPU back to speed after that pause.
     clocks = ClockSampler(local)
+    # Warm-up and soak steps hold the previous step's outputs until the next step
+    # returns, as the timed loop does (it keeps them for --verify): the allocator's
+    # pool then already holds the blocks the timed steps need, and no device
+    # allocation lands inside the timed region.
+    last = None
     for _ in range(args.warmup):
         if flush is not None:
             flush.fill_(1)
-        step(x, cfg["causal"])
+        last = step(x, cfg["causal"])
     _lib.check_device_errors(device)
     # then untimed steps until the clocks settle under sustained load, so that every N's
     # timed region (4 s at one GPU, under a second at eight) starts in the same state
