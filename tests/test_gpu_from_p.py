@@ -18,7 +18,7 @@ from ttt_kernels import backward_stubs as bs
 
 pytestmark = pytest.mark.gpu
 TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
-SHAPES = [(1, 1, 64), (1, 2, 200), (2, 1, 257), (1, 1, 512)]
+SHAPES = [(1, 1, 64), (1, 2, 200), (2, 1, 257), (1, 1, 512), (1, 1, 1), (1, 2, 17), (1, 1, 129)]
 
 
 def _case(b, h, t, d, dtype, causal, seed):
