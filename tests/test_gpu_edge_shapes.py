@@ -77,3 +77,34 @@ def test_ragged_lengths_probabilities(t, causal, d):
         assert int((p[..., upper] != 0).sum()) == 0
     ref = orc.math_gradgrad(*(inp[n].detach().cpu().double() for n in NAMES), causal=causal)
     assert orc.normalized_err(o.float().cpu(), ref["o"]) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("d,dtype,shape", [
+    (64, torch.float16, (1, 2, 384)),
+    (128, torch.bfloat16, (1, 2, 384)),
+    (64, torch.float16, (1, 1, 2048)),   # causal: split forward, shares with very different row maxima
+])
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+def test_growing_row_max(d, dtype, shape, causal):
+    """Keys whose norm grows along the sequence, so that a row's running max rises by far
+    more than 2^8 (log2 domain) after its first key tiles: the forward's conditional O
+    rescale runs, several times per row, and split shares carry maxima far apart."""
+    b, h, t = shape
+    inp = orc.seeded_inputs(b, h, t, d, seed=77 + t + d, scale_in=0.5)
+    ramp = torch.linspace(0.25, 16.0, t, dtype=inp["k"].dtype).view(1, 1, t, 1)
+    inp["k"] = inp["k"] * ramp
+    inp = {n: x.to(dtype).cuda() for n, x in inp.items()}
+    scale = 1.0 / math.sqrt(d)
+    s2 = (inp["q"].float() @ inp["k"].float().transpose(-1, -2)) * scale * math.log2(math.e)
+    assert (s2[..., -1].abs().max() - s2[..., 0].abs().max()).item() > 8  # past the rescale threshold (2^8)
+    q, k, v = inp["q"], inp["k"], inp["v"]
+    o, lse2, _ = _lib.attn_fwd(q, k, v, causal, scale)
+    dq, dk, dv, delta = _lib.attn_bwd(q, k, v, o, inp["do"], lse2, causal, scale)
+    gq, gk, gv, gdo = _lib.attn_bwd2(q, k, v, inp["do"], lse2, delta, inp["uq"], inp["uk"], inp["uv"], causal, scale,
+                                     need_gdout=True)
+    torch.cuda.synchronize()
+    ref = orc.math_gradgrad(*(inp[n].detach().cpu().double() for n in NAMES), causal=causal, need_gdo=True)
+    got = {"o": o, "dq": dq, "dk": dk, "dv": dv, "gq": gq, "gk": gk, "gv": gv, "gdo": gdo}
+    for name, x in got.items():
+        err = orc.normalized_err(x.detach().float().cpu(), ref[name])
+        assert err <= TOL[dtype], f"{name}: normalized max-abs error {err:.3e} > {TOL[dtype]:.0e}"
