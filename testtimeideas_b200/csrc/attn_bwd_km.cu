@@ -148,6 +148,15 @@ struct KmCfg {
   static constexpr int BAR_BYTES = (NBAR + 1) * 8;
   static constexpr int FIXED = NR * TILE_R + DS_BYTES + BAR_BYTES + (STAGE_TX - STAGE);
   static constexpr int NSTAGE = (FIXED + 4 * STAGE + 1024 <= 232448) ? 4 : (FIXED + 3 * STAGE + 1024 <= 232448) ? 3 : 2;
+  // Three issuers (d=128 double backward): a stage arrives in two parts on two
+  // barriers, [Q; u_q] and the statistics first (issuer 0's score products and the
+  // elementwise warps), then dO (issuers 1 and 2), so the next tile's first score
+  // products need not wait for the whole stage. The second part uses the l_full
+  // slots that a two-stage ring leaves free.
+  static constexpr bool SPLIT_STAGE = THREE_ISSUERS;
+  static_assert(!SPLIT_STAGE || NSTAGE <= 2, "split stages use the free l_full slots 2, 3");
+  static constexpr int STAGE_TX_A = SPLIT_STAGE ? ST0_BYTES + NSTAT * STAT_BYTES : STAGE_TX;
+  static constexpr int STAGE_TX_B = ST1_BYTES;
   static constexpr int OFF_R = 0;
   static constexpr int OFF_DS = OFF_R + NR * TILE_R;
   static constexpr int OFF_S = OFF_DS + DS_BYTES;
@@ -188,6 +197,8 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
   uint64_t* l_full = bars + 1;    // [4]
+  // SPLIT_STAGE: dO of stage s arrives on l_full_b[s] (l_full[s] has the rest)
+  uint64_t* l_full_b = C::SPLIT_STAGE ? l_full + 2 : l_full;
   uint64_t* l_empty = bars + 5;   // [4]
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_free = bars + 11;   // [2] (NCT arrivals)
@@ -320,21 +331,38 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
         const int s = n % NSTAGE;
         const int qrow = (qt0 + n) * BM;
         if (n >= NSTAGE && !mbar_wait(l_empty + s, ((n / NSTAGE) - 1) & 1, g, 1)) break;
-        mbar_arrive_tx(l_full + s, C::STAGE_TX);
-        // str[0] = Q, str[1] = dO, str[2] = u_q (stacked under Q)
-        for (int pp = 0; pp < NP; ++pp) {
-          tma_load_4d(st0(s) + pp * SR0 * 128, &p.str[0], l_full + s, pp * 64, qrow, hidx, bidx);
-          tma_load_4d(st1(s) + pp * BM * 128, &p.str[1], l_full + s, pp * 64, qrow, hidx, bidx);
-          if constexpr (C::BWD2)
+        if constexpr (C::SPLIT_STAGE) {
+          // [Q; u_q] and the statistics first, then dO, each part on its own barrier
+          mbar_arrive_tx(l_full + s, C::STAGE_TX_A);
+          for (int pp = 0; pp < NP; ++pp) {
+            tma_load_4d(st0(s) + pp * SR0 * 128, &p.str[0], l_full + s, pp * 64, qrow, hidx, bidx);
             tma_load_4d(st0(s) + pp * SR0 * 128 + BM * 128, &p.str[2], l_full + s, pp * 64, qrow, hidx, bidx);
+          }
+          for (int t = 0; t < C::NSTAT; ++t)
+            tma_load_2d(const_cast<float*>(statS(s, t)), &p.st[t], l_full + s, qrow, bh);
+          mbar_arrive_tx(l_full_b + s, C::STAGE_TX_B);
+          for (int pp = 0; pp < NP; ++pp)
+            tma_load_4d(st1(s) + pp * BM * 128, &p.str[1], l_full_b + s, pp * 64, qrow, hidx, bidx);
+        } else {
+          mbar_arrive_tx(l_full + s, C::STAGE_TX);
+          // str[0] = Q, str[1] = dO, str[2] = u_q (stacked under Q)
+          for (int pp = 0; pp < NP; ++pp) {
+            tma_load_4d(st0(s) + pp * SR0 * 128, &p.str[0], l_full + s, pp * 64, qrow, hidx, bidx);
+            tma_load_4d(st1(s) + pp * BM * 128, &p.str[1], l_full + s, pp * 64, qrow, hidx, bidx);
+            if constexpr (C::BWD2)
+              tma_load_4d(st0(s) + pp * SR0 * 128 + BM * 128, &p.str[2], l_full + s, pp * 64, qrow, hidx, bidx);
+          }
+          for (int t = 0; t < C::NSTAT; ++t)
+            tma_load_2d(const_cast<float*>(statS(s, t)), &p.st[t], l_full + s, qrow, bh);
         }
-        for (int t = 0; t < C::NSTAT; ++t)
-          tma_load_2d(const_cast<float*>(statS(s, t)), &p.st[t], l_full + s, qrow, bh);
         issued[s] = n + 1;
       }
       mbar_drain(res_full, 0);
       for (int s = 0; s < NSTAGE; ++s)
-        if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
+        if (issued[s] > 0) {
+          mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
+          if constexpr (C::SPLIT_STAGE) mbar_drain(l_full_b + s, ((issued[s] - 1) / NSTAGE) & 1);
+        }
     }
    } else if (warp == WARP_MMA || ((C::TWO_ISSUERS || C::THREE_ISSUERS) && warp == WARP_MMA2) ||
               (C::THREE_ISSUERS && warp == WARP_MMA3)) {
@@ -496,7 +524,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
             const int sp = (n - 1) % NSTAGE;
             const uint32_t bQ = smem_u32(st0(sp)), bDO = smem_u32(st1(sp)), bUQ = bQ + BM * 128;
             const uint32_t acc_first = n > 1 ? 1u : 0u;
-            const uint64_t* pbar = n < n_tiles ? l_full + s : done;
+            const uint64_t* pbar = n < n_tiles ? l_full_b + s : done;
             const uint32_t ppar = n < n_tiles ? static_cast<uint32_t>((n / NSTAGE) & 1) : 0u;
             static_assert(BM / 16 == 4, "the batched accumulate issue covers four K-steps");
             uint32_t seen;
@@ -514,7 +542,7 @@ __global__ void __launch_bounds__(KmCfg<D, KIND>::NTHREADS, 1) attn_km_kernel(co
           }
           if (n < n_tiles) {
             // dP^T = V dO^T (issuer 1) or (dO u_v^T)^T = u_v dO^T (issuer 2) over the E just read
-            if (!stage_seen && !(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
+            if (!stage_seen && !(ok = mbar_wait(l_full_b + s, (n / NSTAGE) & 1, g, 2))) break;
             tc_fence_after();
             const uint32_t b1 = smem_u32(st1(s)), a0 = me == 1 ? aV : aUV;
             const uint32_t dcol = tmem + (me == 1 ? C::C_DP : C::C_UV);
