@@ -98,6 +98,11 @@ struct QmCfg {
   static_assert(TMEM_USED <= 512, "TMEM overflow");
   static constexpr int FIXED = NR_SMEM * TILE_R + E_BYTES + 16 * 8 + 16 + 1024;
   static constexpr int NSTAGE = (FIXED + 4 * STAGE <= 232448) ? 4 : (FIXED + 3 * STAGE <= 232448) ? 3 : 2;
+  // Statistics pass with a two-stage ring (d = 128): a stage arrives in two parts
+  // on two barriers, [K; u_k] first (the key-side score products), then [V; u_v],
+  // so a tile's first products need not wait for the whole stage. The second part
+  // uses the l_full slots that a two-stage ring leaves free.
+  static constexpr bool SPLIT_STAGE = KIND == kStats && NSTAGE == 2;
   static constexpr int OFF_R = 0;
   static constexpr int OFF_S = OFF_R + NR_SMEM * TILE_R;
   static constexpr int OFF_E = OFF_S + NSTAGE * STAGE;
@@ -128,6 +133,8 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
   uint64_t* l_full = bars + 1;   // [4] TMA -> MMA
+  // SPLIT_STAGE: [V; u_v] of stage s arrives on l_full_b[s] (l_full[s] has [K; u_k])
+  uint64_t* l_full_b = C::SPLIT_STAGE ? l_full + 2 : l_full;
   uint64_t* l_empty = bars + 5;  // [4] MMA -> TMA
   uint64_t* s_full = bars + 9;   // [2] MMA -> compute
   uint64_t* s_free = bars + 11;  // [2] compute -> MMA (NCT arrivals)
@@ -221,18 +228,34 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       for (int n = 0; n < n_tiles; ++n) {
         const int s = n % NSTAGE;
         if (n >= NSTAGE && !mbar_wait(l_empty + s, ((n / NSTAGE) - 1) & 1, g, 1)) break;
-        mbar_arrive_tx(l_full + s, NSTR * BN * D * 2);
-        // str[0] = K, str[1] = V, str[2] = u_k, str[3] = u_v
-        for (int t = 0; t < NSTR; ++t) {
-          uint8_t* dst = tileS(s, t & 1) + (t >> 1) * BN * 128;
-          for (int pp = 0; pp < NP; ++pp)
-            tma_load_4d(dst + pp * SR * 128, &p.str[t], l_full + s, pp * 64, (n_first + n) * BN, hidx, bidx);
+        if constexpr (C::SPLIT_STAGE) {
+          // [K; u_k] on l_full[s], then [V; u_v] on l_full_b[s]
+          for (int part = 0; part < 2; ++part) {
+            uint64_t* bar = part ? l_full_b + s : l_full + s;
+            mbar_arrive_tx(bar, 2 * BN * D * 2);
+            for (int t = part; t < NSTR; t += 2) {
+              uint8_t* dst = tileS(s, t & 1) + (t >> 1) * BN * 128;
+              for (int pp = 0; pp < NP; ++pp)
+                tma_load_4d(dst + pp * SR * 128, &p.str[t], bar, pp * 64, (n_first + n) * BN, hidx, bidx);
+            }
+          }
+        } else {
+          mbar_arrive_tx(l_full + s, NSTR * BN * D * 2);
+          // str[0] = K, str[1] = V, str[2] = u_k, str[3] = u_v
+          for (int t = 0; t < NSTR; ++t) {
+            uint8_t* dst = tileS(s, t & 1) + (t >> 1) * BN * 128;
+            for (int pp = 0; pp < NP; ++pp)
+              tma_load_4d(dst + pp * SR * 128, &p.str[t], l_full + s, pp * 64, (n_first + n) * BN, hidx, bidx);
+          }
         }
         issued[s] = n + 1;
       }
       mbar_drain(res_full, 0);
       for (int s = 0; s < NSTAGE; ++s)
-        if (issued[s] > 0) mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
+        if (issued[s] > 0) {
+          mbar_drain(l_full + s, ((issued[s] - 1) / NSTAGE) & 1);
+          if constexpr (C::SPLIT_STAGE) mbar_drain(l_full_b + s, ((issued[s] - 1) / NSTAGE) & 1);
+        }
     }
    } else if (warp == WARP_MMA || (C::TWO_ISSUERS && warp == WARP_MMA2)) {
     // ------------------------------------------------------------ MMA issuer(s)
@@ -248,8 +271,10 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
       // parts: bit 0 the products on the key side ([S | Q u_k^T], u_q K^T, or S),
       // bit 1 those on the value side ([dP | dO u_v^T], or dP); each part is one
       // issuer's when two issue (see TWO_ISSUERS). The probes ride on the value side.
+      // With SPLIT_STAGE the value side first waits for its part of the stage; a wait that
+      // gives up clears *stage_ok and returns before any value-side product or commit.
       auto issue_scores = [&](int n, const uint64_t* bar0, uint32_t par0, const uint64_t* bar1, uint32_t par1,
-                              int parts = 3) -> uint32_t {
+                              int parts = 3, bool* stage_ok = nullptr) -> uint32_t {
         const int sb = n % NBUF, s = n % NSTAGE;
         const uint32_t base = tmem + sb * C::NSC * BN;
         const uint32_t b0 = smem_u32(tileS(s, 0)), b1 = smem_u32(tileS(s, 1));
@@ -273,9 +298,17 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
                 umma_ss(base + C::C_GDS, desc_kmajor(aUQ, BM, kk), desc_kmajor(b0, SR, kk), id_n1, 1u);
             }
           }
-          if (parts & 2)
+          if (parts & 2) {
+            if constexpr (C::SPLIT_STAGE) {
+              if (!mbar_wait(l_full_b + s, (n / NSTAGE) & 1, g, 2)) {
+                *stage_ok = false;
+                return 0u;
+              }
+              tc_fence_after();
+            }
             seen = issue_ss<D / 16, LS>(base + C::C_DP, desc_kmajor(aDO, BM, 0), desc_kmajor(b1, SR, 0), id_n2, 0u,
                                         bar0, par0, bar1, par1);
+          }
         } else if constexpr (C::RT_Q && C::RT_DO) {
           if (parts & 1) {
 #pragma unroll
@@ -348,7 +381,7 @@ __global__ void __launch_bounds__(QmCfg<D, KIND, GDO>::NTHREADS, 1) attn_qm_kern
             if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 2))) break;
             if (n >= NBUF && !(ok = mbar_wait(s_free + sb, ((n / NBUF) - 1) & 1, g, 3))) break;
             tc_fence_after();
-            issue_scores(n, done, 0u, done, 0u);
+            issue_scores(n, done, 0u, done, 0u, 3, &ok);
           }
         } else {
           // issuer 0: the score products of every tile (with SPLIT_SCORES the key-side
