@@ -79,6 +79,11 @@ struct FpCfg {
   // kFpDK: the streamed queries' rowsums of each step, staged by the producer
   // warp (W floats per stage slot, outside the 1024-aligned stages)
   static constexpr bool RS_RING = RS_PER > 0;
+  // kFpDK with a two-stage ring (d = 128): a stage arrives in two parts on two
+  // barriers, dO first (the score product's operand), then P, Q and the rowsums,
+  // so the step's score product need not wait for the whole stage. The second
+  // part uses the l_full slots that a two-stage ring leaves free.
+  static constexpr bool SPLIT_STAGE = MODE == kFpDK && NSTAGE == 2;
   static constexpr int RS_BYTES = NSTAGE * RS_PER;
   static constexpr int OFF_R = 0;
   static constexpr int OFF_S = OFF_R + NR * TILE_R;
@@ -118,6 +123,8 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* res_full = bars + 0;
   uint64_t* l_full = bars + 1;    // [4]
+  // SPLIT_STAGE: P, Q and the rowsums of stage s arrive on l_full_b[s] (l_full[s] has dO)
+  uint64_t* l_full_b = C::SPLIT_STAGE ? l_full + 2 : l_full;
   uint64_t* l_empty = bars + 5;   // [4] (ELEM: both MMA threads commit)
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_free = bars + 11;   // [2] (NCT arrivals)
@@ -155,8 +162,14 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
     }
     if constexpr (C::ELEM)
       for (int i = 0; i < 4; ++i) mbar_init(l_empty + i, 2);
-    if constexpr (C::RS_RING)  // the TMA arrival and the producer warp's rowsum copy
+    if constexpr (C::SPLIT_STAGE) {  // dO alone; then the TMA arrival and the rowsum copy
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(l_full + i, 1);
+        mbar_init(l_full_b + i, 2);
+      }
+    } else if constexpr (C::RS_RING) {  // the TMA arrival and the producer warp's rowsum copy
       for (int i = 0; i < 4; ++i) mbar_init(l_full + i, 2);
+    }
     *abort_flag = (p.err != nullptr && *reinterpret_cast<volatile int*>(p.err) != 0) ? 1 : 0;
     fence_mbar_init();
   }
@@ -206,15 +219,27 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
       if (lane == 0) {
         if (n >= NSTAGE) ok = mbar_wait(l_empty + s, ((n / NSTAGE) - 1) & 1, g, 1);
         if (ok) {
-          mbar_arrive_tx(l_full + s, C::STAGE_TX);
-          // P tile: 64-column panels of P_ROWS rows
           int pcol, prow;
           p_coords(n, pcol, prow);
-          for (int pp = 0; pp < C::P_COLS / 64; ++pp)
-            tma_load_4d(tileP(s) + pp * C::P_ROWS * 128, &p.str[0], l_full + s, pcol + pp * 64, prow, hidx, bidx);
-          for (int i = 0; i < C::NX; ++i)
+          if constexpr (C::SPLIT_STAGE) {
+            // dO on l_full[s]; P and Q on l_full_b[s]
+            mbar_arrive_tx(l_full + s, C::TILE_X);
             for (int pp = 0; pp < NP; ++pp)
-              tma_load_4d(tileX(s, i) + pp * W * 128, &p.str[1 + i], l_full + s, pp * 64, j0, hidx, bidx);
+              tma_load_4d(tileX(s, 0) + pp * W * 128, &p.str[1], l_full + s, pp * 64, j0, hidx, bidx);
+            mbar_arrive_tx(l_full_b + s, C::TILE_P + C::TILE_X);
+            for (int pp = 0; pp < C::P_COLS / 64; ++pp)
+              tma_load_4d(tileP(s) + pp * C::P_ROWS * 128, &p.str[0], l_full_b + s, pcol + pp * 64, prow, hidx, bidx);
+            for (int pp = 0; pp < NP; ++pp)
+              tma_load_4d(tileX(s, 1) + pp * W * 128, &p.str[2], l_full_b + s, pp * 64, j0, hidx, bidx);
+          } else {
+            mbar_arrive_tx(l_full + s, C::STAGE_TX);
+            // P tile: 64-column panels of P_ROWS rows
+            for (int pp = 0; pp < C::P_COLS / 64; ++pp)
+              tma_load_4d(tileP(s) + pp * C::P_ROWS * 128, &p.str[0], l_full + s, pcol + pp * 64, prow, hidx, bidx);
+            for (int i = 0; i < C::NX; ++i)
+              for (int pp = 0; pp < NP; ++pp)
+                tma_load_4d(tileX(s, i) + pp * W * 128, &p.str[1 + i], l_full + s, pp * 64, j0, hidx, bidx);
+          }
           if (C::PF > 0 && n + NSTAGE + C::PF < n_tiles) prefetch_p(n + NSTAGE + C::PF);
         }
       }
@@ -229,14 +254,17 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
         v.w = q + 3 < T ? __ldg(rs + q + 3) : 0.f;
         if (lane * 4 < W) reinterpret_cast<float4*>(sRS + s * W)[lane] = v;
         __syncwarp();
-        if (lane == 0) mbar_arrive(l_full + s);
+        if (lane == 0) mbar_arrive(l_full_b + s);
       } else {
         if (!ok) break;
       }
     }
     if (lane == 0) {
       if constexpr (C::NR > 0) mbar_drain(res_full, 0);
-      for (int j = max(0, n - NSTAGE); j < n; ++j) mbar_drain(l_full + j % NSTAGE, (j / NSTAGE) & 1);
+      for (int j = max(0, n - NSTAGE); j < n; ++j) {
+        mbar_drain(l_full + j % NSTAGE, (j / NSTAGE) & 1);
+        if constexpr (C::SPLIT_STAGE) mbar_drain(l_full_b + j % NSTAGE, (j / NSTAGE) & 1);
+      }
     }
   } else if (warp == C::WARP_MMA && !C::ELEM) {
     // ------------------------------------------------------------ MMA issuer (pure products)
@@ -293,7 +321,7 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
         const int s = n % NSTAGE, eb = n & 1;
         if (!(ok = mbar_wait(e_full + eb, (n >> 1) & 1, g, 5))) break;
         // the stage's tiles landed (already observed by the elementwise warps)
-        if (!(ok = mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 5))) break;
+        if (!(ok = mbar_wait(l_full_b + s, (n / NSTAGE) & 1, g, 5))) break;
         tc_fence_after();
         const uint32_t bX = smem_u32(tileX(s, 1));
 #pragma unroll
@@ -328,7 +356,7 @@ __global__ void __launch_bounds__(FpCfg<D, MODE>::NTHREADS, 1) attn_from_p_kerne
         reg_fence(dp);
         tc_fence_before();
         mbar_arrive(s_free + sb);
-        if (!mbar_wait(l_full + s, (n / NSTAGE) & 1, g, 7)) { ok = false; break; }
+        if (!mbar_wait(l_full_b + s, (n / NSTAGE) & 1, g, 7)) { ok = false; break; }
         if (n >= 2 && !mbar_wait(e_empty + eb, ((n >> 1) - 1) & 1, g, 8)) { ok = false; break; }
         const uint8_t* tp = tileP(s);
         const uint32_t te = tmem + lane_off + C::C_E + eb * (W / 2) + half * (CW / 2);
