@@ -31,7 +31,8 @@
 // compute warps have read the previous contents of that TMEM buffer (s_free);
 // tile n-1's accumulate products once its elementwise results are in shared
 // memory (e_full). Streamed tiles use a 2..4-stage TMA ring sized from the
-// shared-memory budget. For the 128-wide double backward the elementwise
+// shared-memory budget; the two-stage ring of the d=128 statistics pass takes
+// each stage in two parts ([K; u_k], then [V; u_v]) on two barriers. For the 128-wide double backward the elementwise
 // results are written into the [V; u_v] part of their own stage, which only the
 // score products read. Causal: key tiles past the diagonal are skipped and only
 // boundary tiles are masked.
